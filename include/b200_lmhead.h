@@ -1,0 +1,101 @@
+/* libb200lmhead.so -- fused SiLU*mul FP8 quant, per-token group FP8 quant, and the FP8 / W4
+ * lm_head GEMVs of the decode hot path, for B200 (sm_100a).
+ *
+ * Plain pointers and sizes, no torch types; every entry returns an int status (0 = ok,
+ * negative = argument error, positive = cudaError_t) except r4d_gemm_w4a16_nt_m64, whose
+ * reference ABI returns void. Nothing allocates; outputs and scratch are caller-owned.
+ *
+ * Packed weight layouts (B200 formats; their codes, scales and zeros are the reference's):
+ *   FP8 wq  e4m3 [N/16 strips][K/128][16 rows][128 B]; 16-byte chunk c of strip row r is
+ *           stored at chunk c ^ (r & 7). ws fp32 [N/128, K/128] row-major (unchanged).
+ *   W4  wq  u32 [N_pad/16][K/128][2][8 g][4 t][4 words]; word w of lane (g, t) holds the
+ *           offset-binary codes of k = 128*kb + 32*w + 8*t + j in nibble (j & 1)*4 + (j >> 1)
+ *           of row 16*strip + 8*half + g.
+ *       wsz int32 [N_pad/16, K/128, 16]: f16 scale | f16(-(1024 + zero)) << 16 (unchanged).
+ */
+#ifndef B200_LMHEAD_H
+#define B200_LMHEAD_H
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Fused silu_and_mul + FP8 quant (replaces the Triton _silu_mul_quant_kernel behind
+ * silu_mul_quant, kernels/fused_silu_mul_quant.py:26-101). x = [rows, 2*d] (gate | up) with
+ * row stride stride_x elements, dtype 0 = bf16, 1 = f16. q e4m3 [rows, d]; group 0: scale fp32
+ * [rows] = max(amax/448, 1/(448*512)) with q = e4m3(clamp(a / scale)); group 128: scale
+ * [rows, d/128] = max(amax_g, 1e-10) * (1/448). act (nullable) [rows, d] in x's dtype.
+ * Returns -1 for d > 8192 or negative sizes, -2 bad dtype, -3 unaligned group-128 call. */
+int b200_silu_mul_quant(const void* x, int rows, int d, long long stride_x, int dtype, void* q,
+                        float* scale, void* act, int group, cudaStream_t stream);
+
+/* per_token_group_quant_fp8(x, group) (vLLM; called at kernels/fp8_target_lmhead.py:73):
+ * s = max(amax, 1e-10) * (1/448), q = e4m3(clamp(x / s)); q [M, K], s [M, K/group]. */
+int b200_per_token_group_quant_fp8(const void* x, int M, int K, long long stride_x, int dtype,
+                                   int group, void* q, float* s, cudaStream_t stream);
+
+/* Bytes of the zero-initialised scratch the fused lm_head entries use (per-CTA row
+ * statistics and a ticket counter); each call leaves it zeroed again. */
+long long b200_lmhead_workspace_bytes(void);
+
+/* Device error word (1 = a bounded pipeline wait timed out); reset != 0 clears it. Synchronous. */
+int b200_lmhead_error(int reset);
+
+/* Fused FP8 target lm_head (replaces gemm_fp8_block = per_token_group_quant_fp8 +
+ * fp8hip_block_scaled_mm, kernels/fp8_target_lmhead.py:70-74, and adds the row statistics).
+ * x bf16 [M, K]; wq / ws packed as above over N rows (N % 128 == 0, K % 128 == 0); y bf16
+ * [M, ldy] (nullable); row_max fp32 [M], row_arg int32 [M] = first argmax + vocab_offset,
+ * row_lse fp32 [M] (each nullable; any of them needs the workspace); qx_out e4m3 [M, K] and
+ * xs_out fp32 [M, K/128] (nullable) receive the quantized activation.
+ * Returns -1 M < 0, -2 N % 128, -3 K % 128, -8 shape exceeds shared memory, -9 workspace
+ * missing / too small, -10 misaligned pointer. */
+int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                    long long vocab_offset, void* y, long long ldy, float* row_max, int* row_arg,
+                    float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                    long long workspace_bytes, cudaStream_t stream);
+
+/* The closed fp8hip GEMM's ABI (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K]
+ * and fp32 xs [M, K/128], packed w / ws, bf16 y [M, N]. */
+int fp8hip_gemm_w8a8_launch(void* qx, void* w, void* xs, void* ws, void* y, int M, int N, int K,
+                            void* stream);
+
+/* hcq_gemm_fp8blk_nt_m16 (kernels/experimental/fp8skinny/hcq_fp8skinny.hip:168-199): the same
+ * operands for M <= 16 with the reference's precondition codes on its launch knobs:
+ * -1 M outside 1..16, -2 N % 128, -3 K % 128, -4 (K/128) % SK, -5 WV*SK*32 > 1024,
+ * -6 NPW not in {1,2,4}, -7 (WV*NPW*SK*256 + 16*K/128)*4 > 64 KB. */
+int hcq_gemm_fp8blk_nt_m16(void* a, void* as, void* w, void* ws, void* c, int M, int K, int N,
+                           int WV, int SK, int NPW, void* stream);
+int hcq_gemm_fp8blk_nt_m16_max_m(void);
+
+/* Read-only bandwidth control (hcq_stream_probe, hcq_fp8skinny.hip:206-224): streams `bytes`
+ * (multiple of 16) from w over `wgs` CTAs; -1 bytes % 16, -2 wgs < 1. */
+int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream);
+
+/* Fused W4 draft lm_head (the math of r4d_gemm_w4a16_nt_m64 behind gemm_w4a16,
+ * kernels/draft_w4_lmhead.py:351-403, plus the row statistics the MTP head reduces,
+ * patches/models/qwen4_exp/amd/mtp.py.diff L194-227). x [M, K] (x_dtype 0 = bf16, rounded to
+ * f16 in the kernel; 1 = f16); wq / wsz packed as above over N_pad rows; rows >= n_valid are
+ * padding (written to y, excluded from the statistics). Same outputs and codes as
+ * b200_fp8_lmhead plus -11 bad dtype. */
+int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+                   int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                   float* row_max, int* row_arg, float* row_lse, void* workspace,
+                   long long workspace_bytes, cudaStream_t stream);
+
+/* r4d_gemm_w4a16_nt_m64 (ABI bound at kernels/draft_w4_lmhead.py:118-127): f16 a [M, K],
+ * M <= 64, packed wq / wsz, bf16 c [M, N] with N = N_pad. WV/SK/MB/NPW/NT are the gfx1201
+ * launch knobs, accepted and ignored. Returns void like the reference; the status of the
+ * last call is r4d_gemm_w4a16_nt_m64_last_error(). */
+void r4d_gemm_w4a16_nt_m64(long a, long wq, long wsz, long c, int M, int K, int N, int WV, int SK,
+                           int MB, int NPW, int NT, long stream);
+int r4d_gemm_w4a16_nt_m64_last_error(void);
+int r4d_gemm_w4a16_nt_m64_max_m(void);  /* 64  (R4D_GEMM_W4_MAX_M) */
+int r4d_gemm_w4a16_nt_m64_group(void);  /* 128 (the quantization group along K) */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_LMHEAD_H */

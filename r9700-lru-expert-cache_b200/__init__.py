@@ -1,0 +1,17 @@
+"""B200-native (sm_100a) rebuild of the quantized decode hot path of
+davetha/r9700-lru-expert-cache, behind the reference's own Python entry points and
+librlu's C ABI:
+
+* ``fused_silu_mul_quant`` -- fused SiLU*mul -> FP8-e4m3 activation quant
+* ``draft_w4_lmhead``      -- W4 group-128 draft lm_head GEMV (+ fused argmax / logsumexp)
+* ``fp8_target_lmhead``    -- FP8 128x128 block-scaled target lm_head (+ fused argmax / lse)
+* ``lru``                  -- device-side LRU expert-slot cache (manage / fused / gather)
+* ``sharded``              -- vocab-sharded lm_head combine and expert-id-sharded LRU
+
+The kernels live in two in-tree shared libraries (librlu.so, libb200lmhead.so) built from
+``csrc/`` by ``build.py``; there is no CPU fallback.
+"""
+from . import _lib  # noqa: F401
+from . import draft_w4_lmhead, fp8_target_lmhead, fused_silu_mul_quant, lru, sharded  # noqa: F401
+
+__all__ = ["draft_w4_lmhead", "fp8_target_lmhead", "fused_silu_mul_quant", "lru", "sharded"]

@@ -1,0 +1,703 @@
+// Small-M lm_head GEMVs for B200 (sm_100a): FP8 128x128 block-scaled and W4 group-128.
+//
+//   FP8: y[m, n] = sum_kb xs[m,kb] * ws[n/128,kb] * sum_{k in kb} qx[m,k] * wq[n,k]
+//        (the operand contract of fp8hip_gemm_w8a8 / hcq_gemm_fp8blk_nt_m16,
+//        kernels/experimental/fp8skinny/hcq_fp8skinny.hip:1-50); with the activation quant
+//        per_token_group_quant_fp8(x, 128) fused into the prologue (kernels/fp8_target_lmhead.py:73).
+//   W4:  y[m, n] = sum_g scale[n,g] * sum_{k in g} f16(x[m,k]) * (q[n,k] - zero[n,g])
+//        (r4d_gemm_w4a16_nt_m64's math, kernels/draft_w4_lmhead.py:4-50), fp32 accumulation.
+//   Optional fused epilogue: per row m, max / first-index argmax / logsumexp over the N
+//   outputs of this call (the local argmax of mtp.py.diff L211-214, plus the logsumexp).
+//
+// Decode M is 1..16 here, so the weight stream is the whole cost. Per CTA (one per SM):
+//   * warp 0 lane 0 streams the CTA's contiguous range of 16-row strips with 1-D bulk async
+//     copies (cp.async.bulk, L2 evict-first) into a ring of shared-memory stages; each stage
+//     is one strip's run of 128-K blocks, contiguous in the packed layout, so one copy fills
+//     it. Full / empty mbarriers carry the hand-off; every wait is bounded by %globaltimer
+//     and reports a timeout through an error word instead of hanging.
+//   * 4 consumer warps take whole strips in turn. A strip is 16 weight rows, which is the A
+//     operand of a warp MMA: FP8 uses mma.sync m16n8k32 e4m3 (128-bit shared loads straight
+//     into A fragments), W4 widens nibbles to f16 in registers with one lop3 + one hadd2 per
+//     pair ((nibble | 0x6400) - (1024 + zero) is exact in f16) and uses m16n8k16 f16. The
+//     activation (<= 16 tokens) is the B operand from shared memory. Block / group scales are
+//     applied in fp32 once per 128-K block.
+//   * the activation prologue (quantize or convert x into shared memory) runs on the
+//     consumer warps while the producer already streams the first stages.
+// The weight never passes through registers of more than one warp and never touches L1; the
+// CTA keeps (stages x stage bytes), ~160 KB, of weight reads in flight.
+//
+// Packed layouts (their own, B200 format; codes / scales / zeros are the reference's):
+//   FP8 wq: [N/16 strips][K/128][16 rows][128 B]; 16-byte chunk c of row r at chunk c^(r&7).
+//   W4  wq: [N/16][K/128][2][8 g][4 t][4 words] u32; word w of lane (g,t) = codes of
+//           k = 128kb + 32w + 8t + j, code j in nibble (j&1)*4 + (j>>1), offset binary.
+//   W4  wsz: int32 [N/16, K/128, 16] = f16 scale | f16(-(1024 + zero)) << 16
+//           (draft_w4_lmhead.py:47-48, unchanged).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int NC = 4;                    // consumer warps
+constexpr int NTHREADS = 32 * (NC + 1);
+constexpr int MAXM = 16;                 // tokens per launch
+constexpr int SMEM_CAP = 227 * 1024;
+constexpr int MAX_STAGES = 8;
+constexpr int FP8_KB_BYTES = 16 * 128;   // one strip x one 128-K block
+constexpr int W4_KB_BYTES = 16 * 64;
+constexpr int W4_SZ_BYTES = 16 * 4;
+constexpr uint64_t WAIT_NS = 2000000000ull;   // 2 s bound on any pipeline wait
+
+enum Kind { FP8_QUANT = 0, FP8_PREQ = 1, W4_BF16 = 2, W4_F16 = 3 };
+
+__device__ int g_lmhead_err = 0;         // 1 = a pipeline wait timed out
+
+struct Params {
+  const void* x;
+  const float* xs_in;
+  int M, K, N, n_valid;
+  long long vocab_offset;
+  const uint8_t* w;
+  const void* wscale;
+  __nv_bfloat16* y;
+  long long ldy;
+  float* row_max;
+  int* row_arg;
+  float* row_lse;
+  uint8_t* qx_out;
+  float* xs_out;
+  unsigned* counter;
+  float* partial;
+  int kps;           // 128-K blocks per stage
+  int nstage;
+  int stage_bytes;
+  int xs_stride;     // bytes per activation row in shared memory
+  int x_off, xs_off, ring_off;
+};
+
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));   // (a & b) | c
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// ---- activation prologue -----------------------------------------------------------------
+
+// FP8: quantize x (bf16 [M, K]) per token group of 128 into shared memory; rows >= M zero.
+// Same formula as b200_per_token_group_quant_fp8 (bit-identical): s = max(amax,1e-10)*(1/448).
+template <int KIND>
+__device__ void load_activation(const Params& p, char* sm, int rows_x) {
+  const int ctid = threadIdx.x - 32;            // consumer thread 0..127
+  const int KB = p.K / 128;
+  uint8_t* X = reinterpret_cast<uint8_t*>(sm + p.x_off);
+  float* xs = reinterpret_cast<float*>(sm + p.xs_off);
+  if (KIND == FP8_QUANT) {
+    const int half = ctid >> 4, hl = ctid & 15;  // 8 half-warps, 16 lanes x 8 elements
+    const unsigned hmask = 0xffffu << (16 * ((ctid >> 4) & 1));
+    const int ngroups = rows_x * KB;
+    for (int gi = half; gi < ngroups; gi += NC * 2) {
+      const int m = gi / KB, kb = gi % KB;
+      uint8_t* dst = X + m * p.xs_stride + kb * 128 + hl * 8;
+      if (m >= p.M) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(0, 0);
+        if (hl == 0) xs[m * KB + kb] = 0.f;
+        continue;
+      }
+      const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.x) + (long long)m * p.K + kb * 128 + hl * 8;
+      const uint4 r = *reinterpret_cast<const uint4*>(src);
+      const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
+      float f[8];
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        f[i] = __bfloat162float(rv[i]);
+        amax = fmaxf(amax, fabsf(f[i]));
+      }
+#pragma unroll
+      for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
+      const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+      uint2 b;
+      b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
+                             fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
+      b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
+                             fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+      *reinterpret_cast<uint2*>(dst) = b;
+      if (hl == 0) xs[m * KB + kb] = sc;
+      if (p.qx_out != nullptr && blockIdx.x == 0) {
+        *reinterpret_cast<uint2*>(p.qx_out + (long long)m * p.K + kb * 128 + hl * 8) = b;
+        if (hl == 0) p.xs_out[m * KB + kb] = sc;
+      }
+    }
+  } else if (KIND == FP8_PREQ) {
+    const int nvec = rows_x * (p.K / 16);
+    for (int i = ctid; i < nvec; i += NC * 32) {
+      const int m = i / (p.K / 16), c = i % (p.K / 16);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (m < p.M) v = *(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) + (long long)m * p.K) + c);
+      *reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16) = v;
+    }
+    for (int i = ctid; i < rows_x * KB; i += NC * 32) {
+      const int m = i / KB;
+      xs[i] = (m < p.M) ? p.xs_in[i] : 0.f;
+    }
+  } else {
+    // W4: f16 activation rows (bf16 input converted with round-to-nearest-even == x.to(f16))
+    const int nvec = rows_x * (p.K / 8);
+    for (int i = ctid; i < nvec; i += NC * 32) {
+      const int m = i / (p.K / 8), c = i % (p.K / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (m < p.M) {
+        const uint4 r = *(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + (long long)m * p.K) + c);
+        if (KIND == W4_BF16) {
+          const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
+          __half h[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(rv[j]));
+          v = *reinterpret_cast<const uint4*>(h);
+        } else {
+          v = r;
+        }
+      }
+      *reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16) = v;
+    }
+  }
+}
+
+// ---- per-strip consumer math ----------------------------------------------------------------
+
+template <int NT8>
+__device__ __forceinline__ void fp8_stage(const Params& p, uint32_t stage, uint32_t xbase,
+                                          const float* xs, int kb0, int nkb, int strip,
+                                          float (&tot)[NT8][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int KB = p.K / 128;
+  const float* ws = static_cast<const float*>(p.wscale) + (long long)(strip >> 3) * KB;
+  const float wsv = (lane < nkb) ? __ldg(ws + kb0 + lane) : 0.f;
+  const uint32_t c0 = ((t ^ g) & 7) * 16, c1 = (((t + 4) ^ g) & 7) * 16;
+  for (int j = 0; j < nkb; ++j) {
+    const float sw = __shfl_sync(0xffffffffu, wsv, j);
+    const uint32_t tile = stage + j * FP8_KB_BYTES;
+    const uint4 A0 = b200::lds128(tile + g * 128 + c0), A1 = b200::lds128(tile + g * 128 + c1);
+    const uint4 B0 = b200::lds128(tile + (g + 8) * 128 + c0), B1 = b200::lds128(tile + (g + 8) * 128 + c1);
+    const uint32_t wa[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
+    const uint32_t wb[8] = {B0.x, B0.y, B0.z, B0.w, B1.x, B1.y, B1.z, B1.w};
+    const int kb = kb0 + j;
+#pragma unroll
+    for (int nt = 0; nt < NT8; ++nt) {
+      const uint32_t xr = xbase + (8 * nt + g) * p.xs_stride + kb * 128;
+      const uint4 X0 = b200::lds128(xr + t * 16), X1 = b200::lds128(xr + (t + 4) * 16);
+      const uint32_t xw[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        b200::mma_e4m3_16832(acc, wa[2 * s], wb[2 * s], wa[2 * s + 1], wb[2 * s + 1], xw[2 * s], xw[2 * s + 1]);
+      const float s0 = sw * xs[(8 * nt + 2 * t) * KB + kb];
+      const float s1 = sw * xs[(8 * nt + 2 * t + 1) * KB + kb];
+      tot[nt][0] = fmaf(acc[0], s0, tot[nt][0]);
+      tot[nt][1] = fmaf(acc[1], s1, tot[nt][1]);
+      tot[nt][2] = fmaf(acc[2], s0, tot[nt][2]);
+      tot[nt][3] = fmaf(acc[3], s1, tot[nt][3]);
+    }
+  }
+}
+
+template <int NT8>
+__device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32_t xbase, int kb0,
+                                         int nkb, float (&tot)[NT8][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t szbase = stage + p.kps * W4_KB_BYTES;
+  for (int j = 0; j < nkb; ++j) {
+    const uint32_t tile = stage + j * W4_KB_BYTES;
+    const uint4 A = b200::lds128(tile + (g * 4 + t) * 16);
+    const uint4 B = b200::lds128(tile + ((8 + g) * 4 + t) * 16);
+    const uint32_t szA = lds32(szbase + j * W4_SZ_BYTES + g * 4);
+    const uint32_t szB = lds32(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
+    const float scA = __half2float(__ushort_as_half((unsigned short)(szA & 0xffffu)));
+    const float scB = __half2float(__ushort_as_half((unsigned short)(szB & 0xffffu)));
+    const uint32_t nzA = (szA >> 16) | (szA & 0xffff0000u);
+    const uint32_t nzB = (szB >> 16) | (szB & 0xffff0000u);
+    const uint32_t wa[4] = {A.x, A.y, A.z, A.w}, wb[4] = {B.x, B.y, B.z, B.w};
+    const int kb = kb0 + j;
+    float acc[NT8][4];
+#pragma unroll
+    for (int nt = 0; nt < NT8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t pa[4], pb[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pa[q] = hadd2_u32(lop3_and_or(wa[w] >> (4 * q), 0x000F000Fu, 0x64006400u), nzA);
+        pb[q] = hadd2_u32(lop3_and_or(wb[w] >> (4 * q), 0x000F000Fu, 0x64006400u), nzB);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt) {
+        const uint4 X = b200::lds128(xbase + (8 * nt + g) * p.xs_stride + (kb * 128 + 32 * w + 8 * t) * 2);
+        b200::mma_f16_16816(acc[nt], pa[0], pb[0], pa[1], pb[1], X.x, X.y);
+        b200::mma_f16_16816(acc[nt], pa[2], pb[2], pa[3], pb[3], X.z, X.w);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT8; ++nt) {
+      tot[nt][0] = fmaf(acc[nt][0], scA, tot[nt][0]);
+      tot[nt][1] = fmaf(acc[nt][1], scA, tot[nt][1]);
+      tot[nt][2] = fmaf(acc[nt][2], scB, tot[nt][2]);
+      tot[nt][3] = fmaf(acc[nt][3], scB, tot[nt][3]);
+    }
+  }
+}
+
+// ---- the kernel ------------------------------------------------------------------------------
+
+template <int KIND, int NT8, bool STATS>
+__global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
+  extern __shared__ __align__(128) char sm[];
+  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  constexpr int KB_BYTES = IS_W4 ? W4_KB_BYTES : FP8_KB_BYTES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = p.K / 128;
+  const int CH = (KB + p.kps - 1) / p.kps;
+  const int nstrips_total = p.N / 16;
+  const int s0 = (int)(((long long)blockIdx.x * nstrips_total) / gridDim.x);
+  const int s1 = (int)(((long long)(blockIdx.x + 1) * nstrips_total) / gridDim.x);
+  const int nst = (s1 - s0) * CH;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+  uint64_t* empty = full + MAX_STAGES;
+  b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + 128);   // [NC][MAXM]
+  int* s_flag = reinterpret_cast<int*>(sm + 128 + NC * MAXM * sizeof(b200::RowStat));
+  char* ring = sm + p.ring_off;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.nstage; ++i) {
+      b200::mbar_init(&full[i], 1);
+      b200::mbar_init(&empty[i], 1);
+    }
+    b200::fence_mbar_init();
+  }
+  __syncthreads();
+  const uint64_t deadline = b200::globaltimer_ns() + WAIT_NS;
+
+  b200::RowStat st[NT8][2];
+#pragma unroll
+  for (int nt = 0; nt < NT8; ++nt) {
+    b200::rowstat_init(st[nt][0]);
+    b200::rowstat_init(st[nt][1]);
+  }
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = b200::l2_policy_evict_first();
+      int issued = 0;
+      bool ok = true;
+      for (int q = 0; q < nst; ++q) {
+        const int slot = q % p.nstage, round = q / p.nstage;
+        if (round > 0 && !b200::mbar_wait_bounded(&empty[slot], (round - 1) & 1, deadline)) {
+          ok = false;
+          break;
+        }
+        const int strip = s0 + q / CH, ch = q % CH;
+        const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
+        const long long blk = (long long)strip * KB + kb0;
+        char* dst = ring + slot * p.stage_bytes;
+        const uint32_t wbytes = nkb * KB_BYTES;
+        const uint32_t sbytes = IS_W4 ? nkb * W4_SZ_BYTES : 0;
+        b200::mbar_arrive_expect_tx(&full[slot], wbytes + sbytes);
+        b200::bulk_g2s_stream(dst, p.w + blk * KB_BYTES, wbytes, &full[slot], pol);
+        if (IS_W4)
+          b200::bulk_g2s(dst + p.kps * W4_KB_BYTES,
+                         static_cast<const uint8_t*>(p.wscale) + blk * W4_SZ_BYTES, sbytes, &full[slot]);
+        ++issued;
+      }
+      if (!ok) atomicExch(&g_lmhead_err, 1);
+      // never leave with copies in flight: the last use of every slot must have landed
+      for (int q = max(0, issued - p.nstage); q < issued; ++q)
+        b200::mbar_wait_bounded(&full[q % p.nstage], (q / p.nstage) & 1, deadline + WAIT_NS);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- consumers ----------------
+    const int cw = warp - 1;
+    load_activation<KIND>(p, sm, 8 * NT8);
+    consumer_bar();
+    const uint32_t xbase = b200::smem_u32(sm + p.x_off);
+    const float* xs = reinterpret_cast<const float*>(sm + p.xs_off);
+    const uint32_t ring_u32 = b200::smem_u32(ring);
+    const int g = lane >> 2, t = lane & 3;
+    bool ok = true;
+    for (int ls = cw; ls < s1 - s0 && ok; ls += NC) {
+      const int strip = s0 + ls;
+      float tot[NT8][4];
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt) tot[nt][0] = tot[nt][1] = tot[nt][2] = tot[nt][3] = 0.f;
+      for (int ch = 0; ch < CH; ++ch) {
+        const int q = ls * CH + ch, slot = q % p.nstage;
+        const bool got = b200::mbar_wait_bounded(&full[slot], (q / p.nstage) & 1, deadline);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint32_t stage = ring_u32 + slot * p.stage_bytes;
+        const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
+        if (IS_W4)
+          w4_stage<NT8>(p, stage, xbase, kb0, nkb, tot);
+        else
+          fp8_stage<NT8>(p, stage, xbase, xs, kb0, nkb, strip, tot);
+        __syncwarp();
+        if (lane == 0) b200::mbar_arrive(&empty[slot]);
+      }
+      if (!ok) break;
+      // epilogue: rows n0+g, n0+g+8 ; tokens 8nt+2t, 8nt+2t+1
+      const int n0 = strip * 16;
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt) {
+        const int m0 = 8 * nt + 2 * t, m1 = m0 + 1;
+        if (p.y != nullptr) {
+          if (m0 < p.M) {
+            p.y[(long long)m0 * p.ldy + n0 + g] = __float2bfloat16_rn(tot[nt][0]);
+            p.y[(long long)m0 * p.ldy + n0 + g + 8] = __float2bfloat16_rn(tot[nt][2]);
+          }
+          if (m1 < p.M) {
+            p.y[(long long)m1 * p.ldy + n0 + g] = __float2bfloat16_rn(tot[nt][1]);
+            p.y[(long long)m1 * p.ldy + n0 + g + 8] = __float2bfloat16_rn(tot[nt][3]);
+          }
+        }
+        if (STATS) {
+          const int ia = n0 + g, ib = n0 + g + 8;
+          const int gia = (int)(ia + p.vocab_offset), gib = (int)(ib + p.vocab_offset);
+          if (ia < p.n_valid) {
+            b200::rowstat_push(st[nt][0], tot[nt][0], gia);
+            b200::rowstat_push(st[nt][1], tot[nt][1], gia);
+          }
+          if (ib < p.n_valid) {
+            b200::rowstat_push(st[nt][0], tot[nt][2], gib);
+            b200::rowstat_push(st[nt][1], tot[nt][3], gib);
+          }
+        }
+      }
+    }
+    if (!ok) atomicExch(&g_lmhead_err, 1);
+    if (STATS) {
+      // merge over the 8 row groups (lanes with equal t), then publish per consumer warp
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int msk = 4; msk < 32; msk <<= 1)
+            st[nt][h] = b200::rowstat_merge(st[nt][h], b200::rowstat_shfl_xor(st[nt][h], msk));
+      if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt) {
+          red[cw * MAXM + 8 * nt + 2 * t] = st[nt][0];
+          red[cw * MAXM + 8 * nt + 2 * t + 1] = st[nt][1];
+        }
+      }
+    }
+  }
+
+  if (!STATS) return;
+  __syncthreads();
+  // ---- CTA partial per token, then the last CTA to finish merges all partials ------------
+  const int G = gridDim.x;
+  if (threadIdx.x < p.M) {
+    const int m = threadIdx.x;
+    b200::RowStat r = red[m];
+    for (int w = 1; w < NC; ++w) r = b200::rowstat_merge(r, red[w * MAXM + m]);
+    float* dst = p.partial + ((long long)m * G + blockIdx.x) * 3;
+    dst[0] = r.m;
+    dst[1] = __int_as_float(r.idx);
+    dst[2] = r.s;
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned ticket = atomicAdd(p.counter, 1u);
+    *s_flag = (ticket == (unsigned)G - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (*s_flag == 0) return;
+  __threadfence();
+  for (int m = warp; m < p.M; m += NC + 1) {
+    b200::RowStat r;
+    b200::rowstat_init(r);
+    for (int c = lane; c < G; c += 32) {
+      const float* src = p.partial + ((long long)m * G + c) * 3;
+      b200::RowStat o;
+      o.m = __ldcg(src);
+      o.idx = __float_as_int(__ldcg(src + 1));
+      o.s = __ldcg(src + 2);
+      r = b200::rowstat_merge(r, o);
+    }
+#pragma unroll
+    for (int msk = 1; msk < 32; msk <<= 1) r = b200::rowstat_merge(r, b200::rowstat_shfl_xor(r, msk));
+    if (lane == 0) {
+      if (p.row_max) p.row_max[m] = r.m;
+      if (p.row_arg) p.row_arg[m] = r.idx;
+      if (p.row_lse) p.row_lse[m] = r.m + logf(r.s);
+    }
+  }
+  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
+}
+
+// ---- read-only stream control (hcq_stream_probe, hcq_fp8skinny.hip:206-224) -----------------
+__global__ void __launch_bounds__(256) stream_probe_kernel(const uint4* __restrict__ w, size_t n16,
+                                                           unsigned* __restrict__ out) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  unsigned acc = 0;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 a = __ldcs(w + i), b = __ldcs(w + i + stride), c = __ldcs(w + i + 2 * stride),
+                d = __ldcs(w + i + 3 * stride);
+    acc ^= a.x ^ a.y ^ a.z ^ a.w ^ b.x ^ b.y ^ b.z ^ b.w ^ c.x ^ c.y ^ c.z ^ c.w ^ d.x ^ d.y ^ d.z ^ d.w;
+  }
+  for (; i < n16; i += stride) {
+    const uint4 a = __ldcs(w + i);
+    acc ^= a.x ^ a.y ^ a.z ^ a.w;
+  }
+  if (acc == 0xdeadbeefu) out[0] = acc;      // never taken in practice; keeps every load live
+}
+
+// ---- host side -------------------------------------------------------------------------------
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+constexpr int HDR = 128 + NC * MAXM * 12 + 16;   // barriers + per-warp stats + flag
+
+// Fill in the shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
+int plan(Params& p, bool is_w4, int nt8) {
+  const int KB = p.K / 128;
+  const int rows_x = 8 * nt8;
+  p.xs_stride = (is_w4 ? 2 * p.K : p.K) + 64;
+  p.xs_off = (HDR + 15) & ~15;
+  p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
+  const int fixed = p.x_off + rows_x * p.xs_stride;
+  const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
+  for (int kps = min(KB, 24); kps >= 1; --kps) {
+    const int sb = (kps * per_kb + 127) & ~127;
+    const int ring_off = (fixed + 127) & ~127;
+    const int nstage = min(MAX_STAGES, (SMEM_CAP - ring_off) / sb);
+    if (nstage >= 3 || (kps == 1 && nstage >= 2)) {
+      p.kps = kps;
+      p.stage_bytes = sb;
+      p.nstage = nstage;
+      p.ring_off = ring_off;
+      return ring_off + nstage * sb;
+    }
+  }
+  return -1;
+}
+
+template <int KIND, int NT8, bool STATS>
+int launch_one(Params p, cudaStream_t stream) {
+  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  const int smem = plan(p, IS_W4, NT8);
+  if (smem < 0) return -8;
+  auto kern = gemv_kernel<KIND, NT8, STATS>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  const int grid = min(p.N / 16, num_sms());
+  kern<<<grid, NTHREADS, smem, stream>>>(p);
+  return (int)cudaGetLastError();
+}
+
+template <int KIND, bool STATS>
+int launch_m(const Params& p, cudaStream_t stream) {
+  return (p.M <= 8) ? launch_one<KIND, 1, STATS>(p, stream) : launch_one<KIND, 2, STATS>(p, stream);
+}
+
+constexpr long long WORKSPACE_BYTES = 16 + 1024LL * MAXM * 12;
+
+// Runs M in chunks of 16 tokens (one weight pass each).
+template <int KIND>
+int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
+  const int M = p.M, KB = p.K / 128;
+  const bool stats = (p.row_max || p.row_arg || p.row_lse);
+  for (int m0 = 0; m0 < M; m0 += MAXM) {
+    Params q = p;
+    q.M = min(MAXM, M - m0);
+    q.x = static_cast<const char*>(p.x) + (long long)m0 * p.K * x_elem_bytes;
+    if (p.xs_in) q.xs_in = p.xs_in + (long long)m0 * KB;
+    if (p.y) q.y = p.y + (long long)m0 * p.ldy;
+    if (p.row_max) q.row_max = p.row_max + m0;
+    if (p.row_arg) q.row_arg = p.row_arg + m0;
+    if (p.row_lse) q.row_lse = p.row_lse + m0;
+    if (p.qx_out) q.qx_out = p.qx_out + (long long)m0 * p.K;
+    if (p.xs_out) q.xs_out = p.xs_out + (long long)m0 * KB;
+    const int rc = stats ? launch_m<KIND, true>(q, stream) : launch_m<KIND, false>(q, stream);
+    if (rc != 0) return rc;
+  }
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+// Bytes of caller-owned workspace the fused entries need (zero-initialised once; every call
+// leaves it zeroed again). Calls that share a workspace must not overlap on the GPU.
+long long b200_lmhead_workspace_bytes(void) { return WORKSPACE_BYTES; }
+
+// Reads (and with reset != 0 clears) the device error word: 1 = a pipeline wait timed out.
+// Synchronous; for tests and diagnostics only.
+int b200_lmhead_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_lmhead_err, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_lmhead_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+// Fused FP8 target lm_head: x bf16 [M, K] is quantized per token group of 128 in the prologue
+// (bit-identical to b200_per_token_group_quant_fp8), then y = (qx*xs) @ (wq*ws)^T over the
+// N rows of this weight, and per row m: row_max / row_arg (first index, + vocab_offset) /
+// row_lse = log sum exp. Every output pointer is nullable. qx_out / xs_out (nullable) receive
+// the quantized activation. wq / ws in the B200 packed layout (see the file header).
+// Returns 0, -1 bad M, -2 N % 128, -3 K % 128, -8 does not fit shared memory, -9 workspace
+// too small / missing when stats are asked for, -10 misaligned pointer, else a CUDA error.
+int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                    long long vocab_offset, void* y, long long ldy, float* row_max, int* row_arg,
+                    float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                    long long workspace_bytes, cudaStream_t stream) {
+  if (M < 0) return -1;
+  if (N <= 0 || N % 128) return -2;
+  if (K <= 0 || K % 128) return -3;
+  if (M == 0) return 0;
+  const bool stats = row_max || row_arg || row_lse;
+  if (stats && (workspace == nullptr || workspace_bytes < WORKSPACE_BYTES)) return -9;
+  if (!aligned16(x) || !aligned16(wq) || (qx_out && !aligned16(qx_out))) return -10;
+  Params p{};
+  p.x = x; p.M = M; p.K = K; p.N = N; p.n_valid = N; p.vocab_offset = vocab_offset;
+  p.w = static_cast<const uint8_t*>(wq); p.wscale = ws;
+  p.y = static_cast<__nv_bfloat16*>(y); p.ldy = ldy > 0 ? ldy : N;
+  p.row_max = row_max; p.row_arg = row_arg; p.row_lse = row_lse;
+  p.qx_out = static_cast<uint8_t*>(qx_out); p.xs_out = xs_out;
+  p.counter = static_cast<unsigned*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
+  return run_chunks<FP8_QUANT>(p, 2, stream);
+}
+
+// fp8hip_gemm_w8a8_launch(qx, w, xs, ws, y, M, N, K, stream) -- the closed fp8hip GEMM's ABI
+// (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K] with fp32 xs [M, K/128],
+// w / ws as above, y bf16 [M, N].
+int fp8hip_gemm_w8a8_launch(void* qx, void* w, void* xs, void* ws, void* y, int M, int N, int K,
+                            void* stream) {
+  if (M < 0) return -1;
+  if (N <= 0 || N % 128) return -2;
+  if (K <= 0 || K % 128) return -3;
+  if (M == 0) return 0;
+  if (!aligned16(qx) || !aligned16(w)) return -10;
+  Params p{};
+  p.x = qx; p.xs_in = static_cast<const float*>(xs); p.M = M; p.K = K; p.N = N; p.n_valid = N;
+  p.w = static_cast<const uint8_t*>(w); p.wscale = ws;
+  p.y = static_cast<__nv_bfloat16*>(y); p.ldy = N;
+  return run_chunks<FP8_PREQ>(p, 1, static_cast<cudaStream_t>(stream));
+}
+
+// hcq_gemm_fp8blk_nt_m16 (kernels/experimental/fp8skinny/hcq_fp8skinny.hip:168-197): same
+// operands, M <= 16, the reference's precondition codes -1..-7 checked on its launch knobs
+// (WV, SK, NPW); the B200 kernel then runs its own launch plan.
+int hcq_gemm_fp8blk_nt_m16(void* a, void* as, void* w, void* ws, void* c, int M, int K, int N,
+                           int WV, int SK, int NPW, void* stream) {
+  if (M < 1 || M > MAXM) return -1;
+  if (N % 128) return -2;
+  if (K % 128) return -3;
+  if (SK < 1 || (K / 128) % SK) return -4;
+  if (WV < 1 || WV * SK * 32 > 1024) return -5;
+  if (NPW != 1 && NPW != 2 && NPW != 4) return -6;
+  const long long smem = ((long long)WV * NPW * SK * 256 + 16LL * (K / 128)) * 4;
+  if (smem > 64 * 1024) return -7;
+  const int rc = fp8hip_gemm_w8a8_launch(a, w, as, ws, c, M, N, K, stream);
+  return rc == 0 ? 0 : (rc > 0 ? rc : -8);
+}
+
+int hcq_gemm_fp8blk_nt_m16_max_m(void) { return MAXM; }
+
+// Read-only control: streams `bytes` from w with 16-byte loads over `wgs` CTAs of 256.
+int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream) {
+  if (bytes % 16) return -1;
+  if (wgs < 1) return -2;
+  stream_probe_kernel<<<wgs, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(w), (size_t)(bytes / 16), static_cast<unsigned*>(out));
+  return (int)cudaGetLastError();
+}
+
+// Fused W4 draft lm_head: x [M, K] (dtype 0 = bf16, converted to f16 in the kernel exactly as
+// x.to(float16); 1 = f16), packed wq / wsz over N_pad rows (multiple of 16); rows >= n_valid
+// are padding (written to y, excluded from the row statistics). Same outputs as
+// b200_fp8_lmhead. Returns 0, -1 bad M, -2 N_pad % 16, -3 K % 128, -8 smem, -9 workspace,
+// -10 alignment, -11 bad dtype.
+int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+                   int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                   float* row_max, int* row_arg, float* row_lse, void* workspace,
+                   long long workspace_bytes, cudaStream_t stream) {
+  if (M < 0) return -1;
+  if (N_pad <= 0 || N_pad % 16) return -2;
+  if (K <= 0 || K % 128) return -3;
+  if (x_dtype != 0 && x_dtype != 1) return -11;
+  if (M == 0) return 0;
+  const bool stats = row_max || row_arg || row_lse;
+  if (stats && (workspace == nullptr || workspace_bytes < WORKSPACE_BYTES)) return -9;
+  if (!aligned16(x) || !aligned16(wq) || !aligned16(wsz)) return -10;
+  Params p{};
+  p.x = x; p.M = M; p.K = K; p.N = N_pad;
+  p.n_valid = (n_valid > 0 && n_valid < N_pad) ? n_valid : N_pad;
+  p.vocab_offset = vocab_offset;
+  p.w = static_cast<const uint8_t*>(wq); p.wscale = wsz;
+  p.y = static_cast<__nv_bfloat16*>(y); p.ldy = ldy > 0 ? ldy : N_pad;
+  p.row_max = row_max; p.row_arg = row_arg; p.row_lse = row_lse;
+  p.counter = static_cast<unsigned*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
+  return x_dtype == 0 ? run_chunks<W4_BF16>(p, 2, stream) : run_chunks<W4_F16>(p, 2, stream);
+}
+
+static int g_w4_last_rc = 0;
+
+// r4d_gemm_w4a16_nt_m64 (ABI bound at kernels/draft_w4_lmhead.py:118-127): f16 a [M, K],
+// packed wq / wsz, bf16 c [M, N] with N = n_pad. WV/SK/MB/NPW/NT are the AMD launch knobs;
+// they are accepted and ignored (the B200 kernel plans its own launch). Returns nothing,
+// like the reference; the status of the last call is r4d_gemm_w4a16_nt_m64_last_error().
+void r4d_gemm_w4a16_nt_m64(long a, long wq, long wsz, long c, int M, int K, int N, int WV, int SK,
+                           int MB, int NPW, int NT, long stream) {
+  (void)WV; (void)SK; (void)MB; (void)NPW; (void)NT;
+  if (M < 1 || M > 64) {
+    g_w4_last_rc = -1;
+    return;
+  }
+  g_w4_last_rc = b200_w4_lmhead(reinterpret_cast<const void*>(a), 1, M, K,
+                                reinterpret_cast<const void*>(wq), reinterpret_cast<const void*>(wsz), N,
+                                N, 0, reinterpret_cast<void*>(c), N, nullptr, nullptr, nullptr, nullptr,
+                                0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int r4d_gemm_w4a16_nt_m64_last_error(void) { return g_w4_last_rc; }
+int r4d_gemm_w4a16_nt_m64_max_m(void) { return 64; }
+int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
+
+}  // extern "C"

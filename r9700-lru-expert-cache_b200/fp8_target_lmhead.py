@@ -1,0 +1,169 @@
+"""FP8-e4m3 target lm_head with 128x128 fp32 block scales: the host-side mirror of
+kernels/fp8_target_lmhead.py (``available``, ``pack_fp8_block``, ``gemm_fp8_block``,
+``Fp8TargetHead``, ``_MAX_M``), backed by the sm_100a kernels of csrc/lmhead.cu.
+
+Quantization (unchanged from the reference, fp8_target_lmhead.py:14-18, 56-65): per
+128(N) x 128(K) block scale = max(amax, 1e-12)/448 and w_q = e4m3(clamp(w/scale)); the
+activation is quantized per token in groups of 128 (per_token_group_quant_fp8), here fused
+into the GEMV prologue.
+
+Layout: the reference stores the weight in gfx1201 WMMA fragment order. The B200 pack stores
+it as 16-row strips, ``[N/16][K/128][16 rows][128 B]`` with the 16-byte chunk c of row r at
+chunk ``c ^ (r & 7)`` -- one bulk copy per strip run for the GEMV, and the 128-byte-swizzled
+K-major tile a tensor-core operand expects. ``unpack_fp8_block`` restores row-major order.
+
+``fp8_lmhead`` is the fused entry BASELINE asks for: logits plus per-row max, argmax and
+logsumexp in the same pass over the weight.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+from ._workspace import workspace
+
+_BLK = 128
+_MAX_M = int(os.environ.get("VLLM_TARGET_FP8_LMHEAD_MAX_M", "64"))
+FP8 = torch.float8_e4m3fn
+
+
+def available() -> bool:
+    """True when the kernels can run here: a CUDA sm_100 device and the library loads."""
+    try:
+        if not torch.cuda.is_available() or torch.cuda.get_device_capability()[0] != 10:
+            return False
+        _lib.lmhead()
+    except Exception:  # noqa: BLE001
+        return False
+    return True
+
+
+def _strip_swizzle(wq_rows: torch.Tensor) -> torch.Tensor:
+    """Row-major e4m3 [R, K] (R % 16 == 0) -> strip layout bytes, viewed [R, K]."""
+    R, K = wq_rows.shape
+    b = wq_rows.view(torch.uint8).reshape(R // 16, 16, K // 128, 8, 16)     # st, r, kb, c, byte
+    r = torch.arange(16, device=b.device).view(1, 16, 1, 1, 1)
+    c = torch.arange(8, device=b.device).view(1, 1, 1, 8, 1)
+    src = (c ^ (r & 7)).expand(R // 16, 16, K // 128, 8, 16)
+    out = torch.gather(b, 3, src)            # out chunk c' = in chunk c' ^ (r & 7)
+    return out.permute(0, 2, 1, 3, 4).contiguous().view(FP8).view(R, K)
+
+
+def unpack_fp8_block(wq: torch.Tensor) -> torch.Tensor:
+    """Strip layout -> row-major e4m3 [N, K] (the inverse of the pack's permutation)."""
+    N, K = wq.shape
+    b = wq.contiguous().view(torch.uint8).reshape(N // 16, K // 128, 16, 8, 16).permute(0, 2, 1, 3, 4)
+    r = torch.arange(16, device=b.device).view(1, 16, 1, 1, 1)
+    c = torch.arange(8, device=b.device).view(1, 1, 1, 8, 1)
+    src = (c ^ (r & 7)).expand(N // 16, 16, K // 128, 8, 16)
+    return torch.gather(b, 3, src).reshape(N, K).view(FP8)
+
+
+@torch.no_grad()
+def pack_fp8_block(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [N, K] -> (strip-packed e4m3 [N, K], fp32 block scales [N/128, K/128]).
+
+    Row-chunked (4096 rows) so the fp32 temporaries stay small, as in the reference."""
+    N, K = w.shape
+    assert N % _BLK == 0 and K % _BLK == 0, (N, K)
+    out = torch.empty(N, K, dtype=FP8, device=w.device)
+    ws = torch.empty(N // _BLK, K // _BLK, dtype=torch.float32, device=w.device)
+    rows = 4096
+    for r0 in range(0, N, rows):
+        r1 = min(N, r0 + rows)
+        wf = w[r0:r1].float().view((r1 - r0) // _BLK, _BLK, K // _BLK, _BLK)
+        amax = wf.abs().amax(dim=(1, 3), keepdim=True).clamp(min=1e-12)
+        scale = amax / 448.0
+        wq = (wf / scale).clamp(-448.0, 448.0).to(FP8).view(r1 - r0, K)
+        out[r0:r1] = _strip_swizzle(wq)
+        ws[r0 // _BLK:r1 // _BLK] = scale.view((r1 - r0) // _BLK, K // _BLK)
+        del wf, amax, scale, wq
+    return out, ws
+
+
+def _check(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor) -> None:
+    _lib.require_cuda("fp8 lm_head", x, wq, ws)
+    if x.dtype != torch.bfloat16 or x.ndim != 2 or not x.is_contiguous():
+        raise ValueError("fp8 lm_head: x must be a contiguous bf16 [M, K] tensor")
+    if wq.dtype != FP8 or wq.shape[1] != x.shape[1] or not wq.is_contiguous():
+        raise ValueError(f"fp8 lm_head: weight {tuple(wq.shape)} {wq.dtype} does not match x {tuple(x.shape)}")
+    if ws.dtype != torch.float32 or ws.shape != (wq.shape[0] // _BLK, wq.shape[1] // _BLK):
+        raise ValueError("fp8 lm_head: ws must be fp32 [N/128, K/128]")
+
+
+def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset: int = 0,
+               want_logits: bool = True, out: torch.Tensor | None = None,
+               debug_quant: bool = False):
+    """Fused quant + GEMV + row statistics.
+
+    Returns (logits bf16 [M, N] | None, row_max fp32 [M], argmax int64 [M] (+ vocab_offset),
+    logsumexp fp32 [M]) and, with ``debug_quant``, the quantized activation (q, scales)."""
+    _check(x, wq, ws)
+    M, K = x.shape
+    N = wq.shape[0]
+    dev = x.device
+    y = None
+    if want_logits:
+        y = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    mx = torch.empty(M, dtype=torch.float32, device=dev)
+    arg = torch.empty(M, dtype=torch.int32, device=dev)
+    lse = torch.empty(M, dtype=torch.float32, device=dev)
+    qx = torch.empty(M, K, dtype=FP8, device=dev) if debug_quant else None
+    xs = torch.empty(M, K // _BLK, dtype=torch.float32, device=dev) if debug_quant else None
+    wsp = workspace(dev)
+    rc = _lib.lmhead().b200_fp8_lmhead(
+        _lib.ptr(x), M, K, _lib.ptr(wq), _lib.ptr(ws), N, int(vocab_offset), _lib.ptr(y),
+        N if y is None else y.stride(0), _lib.ptr(mx), _lib.ptr(arg), _lib.ptr(lse),
+        _lib.ptr(qx), _lib.ptr(xs), _lib.ptr(wsp), wsp.numel(), _lib.stream_ptr())
+    _lib.check(rc, "b200_fp8_lmhead")
+    res = (y, mx, arg.to(torch.int64), lse)
+    return res + (qx, xs) if debug_quant else res
+
+
+def gemm_fp8_block(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor) -> torch.Tensor:
+    """bf16 [M, K] @ dequant(W)^T -> bf16 [M, N]; the caller guarantees M <= _MAX_M
+    (fp8_target_lmhead.py:70-74). The activation quant runs inside the kernel."""
+    _check(x, wq, ws)
+    M, K = x.shape
+    y = torch.empty(M, wq.shape[0], dtype=torch.bfloat16, device=x.device)
+    rc = _lib.lmhead().b200_fp8_lmhead(
+        _lib.ptr(x), M, K, _lib.ptr(wq), _lib.ptr(ws), wq.shape[0], 0, _lib.ptr(y), y.stride(0),
+        None, None, None, None, None, None, 0, _lib.stream_ptr())
+    _lib.check(rc, "b200_fp8_lmhead")
+    return y
+
+
+def fp8_block_scaled_mm(qx: torch.Tensor, wq: torch.Tensor, xs: torch.Tensor,
+                        ws: torch.Tensor) -> torch.Tensor:
+    """Pre-quantized operands through fp8hip_gemm_w8a8_launch's ABI -> bf16 [M, N]."""
+    _lib.require_cuda("fp8_block_scaled_mm", qx, wq, xs, ws)
+    M, K = qx.shape
+    N = wq.shape[0]
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=qx.device)
+    rc = _lib.lmhead().fp8hip_gemm_w8a8_launch(_lib.ptr(qx), _lib.ptr(wq), _lib.ptr(xs),
+                                               _lib.ptr(ws), _lib.ptr(y), M, N, K, _lib.stream_ptr())
+    _lib.check(rc, "fp8hip_gemm_w8a8_launch")
+    return y
+
+
+class Fp8TargetHead:
+    """Drop-in replacement for the lm_head's quant_method.apply at decode M
+    (fp8_target_lmhead.py:77-93)."""
+
+    def __init__(self, orig_method, weight: torch.Tensor):
+        self.orig = orig_method
+        self.wq, self.ws = pack_fp8_block(weight)
+        self.n_fp8 = 0
+
+    def apply(self, layer, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        flat = x.reshape(-1, x.shape[-1])
+        if flat.shape[0] > _MAX_M or bias is not None or x.dtype != torch.bfloat16:
+            return self.orig.apply(layer, x, bias=bias)
+        y = gemm_fp8_block(flat.contiguous(), self.wq, self.ws)
+        self.n_fp8 += 1
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+    def __getattr__(self, name):        # everything else passes through to the original
+        return getattr(self.orig, name)

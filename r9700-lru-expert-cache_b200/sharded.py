@@ -1,0 +1,74 @@
+"""Multi-GPU layout of the hot path: one process per GPU, torch.distributed for the plumbing.
+
+lm_head (FP8 target or W4 draft): the vocabulary is split on 128-row block boundaries, so a
+shard is a contiguous slice of the packed weight and of its block scales (1187 blocks of the
+151936-row head -> 149/148 per GPU at 8). Each rank runs the fused GEMV on its shard with
+``vocab_offset`` = its first row and gets (max, argmax, logsumexp) per token row; one
+all-gather of those 3 numbers per row (a [M, 3] float64 tensor, exact for the index) and a
+local combine give the global result:
+    gmax = max_r max_r;   argmax = argmax of the first rank attaining gmax (shards are in
+    vocabulary order, so this is the first global index: the reference's tie rule,
+    mtp.py.diff L223-226);   lse = gmax + log sum_r exp(lse_r - gmax).
+
+Expert cache: experts are split by id, ``experts_per_rank`` each. A rank's cache sees the
+routing shifted by ``-rank * experts_per_rank``; ids outside [0, E_local) are ignored by the
+kernel (r4d_lru.hip:218), so the shift is the whole partition. No collective: every rank
+updates its own slots.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+BLK = 128
+
+
+def vocab_shards(n_rows: int, world: int, blk: int = BLK) -> list[tuple[int, int]]:
+    """Contiguous [r0, r1) row ranges on `blk`-row boundaries, sizes differing by <= 1 block."""
+    assert n_rows % blk == 0, n_rows
+    nb = n_rows // blk
+    out = []
+    for r in range(world):
+        b0 = (r * nb) // world
+        b1 = ((r + 1) * nb) // world
+        out.append((b0 * blk, b1 * blk))
+    return out
+
+
+def combine_row_stats_local(parts):
+    """Combine per-shard (max fp32 [M], argmax int64 [M], lse fp32 [M]) tuples, given in
+    shard (vocabulary) order."""
+    mx = torch.stack([p[0].double() for p in parts])        # [R, M]
+    ar = torch.stack([p[1].to(torch.int64) for p in parts])
+    ls = torch.stack([p[2].double() for p in parts])
+    return _combine(mx, ar, ls)
+
+
+def _combine(mx: torch.Tensor, ar: torch.Tensor, ls: torch.Tensor):
+    gmax, _ = mx.max(dim=0)
+    first = (mx == gmax.unsqueeze(0)).to(torch.int8).argmax(dim=0)     # first rank at gmax
+    arg = ar.gather(0, first.unsqueeze(0)).squeeze(0)
+    lse = gmax + torch.log(torch.exp(ls - gmax.unsqueeze(0)).sum(dim=0))
+    return gmax.float(), arg, lse.float()
+
+
+def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, group=None):
+    """All-gather this rank's per-row (max, argmax, lse) and combine: [M, 3] float64 per
+    rank (24 B/row) in one collective; every rank returns the global triple."""
+    world = dist.get_world_size(group)
+    local = torch.stack([mx.double(), arg.double(), lse.double()], dim=1).contiguous()
+    gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(gathered, local, group=group)
+    return _combine(gathered[:, :, 0], gathered[:, :, 1].to(torch.int64), gathered[:, :, 2])
+
+
+def shard_fp8_head(wq: torch.Tensor, ws: torch.Tensor, rank: int, world: int):
+    """(wq_shard, ws_shard, vocab_offset) for this rank from a packed FP8 head."""
+    r0, r1 = vocab_shards(wq.shape[0], world)[rank]
+    return wq[r0:r1], ws[r0 // BLK:r1 // BLK], r0
+
+
+def local_expert_ids(topk_ids: torch.Tensor, rank: int, experts_per_rank: int) -> torch.Tensor:
+    """Routing as seen by the cache of `rank`: ids shifted into [0, experts_per_rank) for the
+    experts this rank owns; every other id falls outside the range and is ignored."""
+    return (topk_ids.to(torch.int32) - rank * experts_per_rank).contiguous()
