@@ -28,6 +28,7 @@ from __future__ import annotations
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 FP8 = torch.float8_e4m3fn
 FP8_MAX = 448.0
@@ -44,12 +45,13 @@ CLIP_GRID = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7, 0.65, 0.6)   # draft_w4_lmhea
 
 def silu_mul(x: torch.Tensor) -> torch.Tensor:
     """``silu_and_mul`` with the storage-dtype rounding of silu before the multiply and of
-    the product on store (fused_silu_mul_quant.py:45-48)."""
+    the product on store (fused_silu_mul_quant.py:45-48): ``F.silu`` on the storage dtype
+    (one fused ``x / (1 + exp(-x))`` in fp32, rounded on store), then the product of the
+    stored values rounded on store. On CUDA tensors this is torch's own silu kernel, the
+    same expression vLLM's act_and_mul_kernel evaluates."""
     d = x.shape[1] // 2
-    g = x[:, :d].float()
-    u = x[:, d:].float()
-    s = (g / (1.0 + torch.exp(-g))).to(x.dtype).float()
-    return (s * u).to(x.dtype)
+    s = F.silu(x[:, :d])
+    return (s.float() * x[:, d:].float()).to(x.dtype)
 
 
 def silu_mul_quant(x: torch.Tensor, write_act: bool = False):
@@ -58,7 +60,9 @@ def silu_mul_quant(x: torch.Tensor, write_act: bool = False):
     a = silu_mul(x)
     af = a.float()
     amax = af.abs().amax(dim=1, keepdim=True) if af.shape[1] else af.new_zeros(af.shape[0], 1)
-    scale = torch.clamp(amax / FP8_MAX, min=MIN_SCALE)
+    # a true division by 448: a tensor divisor (torch turns a Python-scalar divisor into a
+    # reciprocal multiply on CUDA, which is not the reference's `amax / FP8_MAX`)
+    scale = torch.clamp_min(amax / torch.full_like(amax, FP8_MAX), MIN_SCALE)
     q = (af / scale).clamp(-FP8_MAX, FP8_MAX).to(FP8)
     return (a if write_act else None), q, scale
 
@@ -67,9 +71,8 @@ def group_quant_fp8(x: torch.Tensor, group: int = BLK, eps: float = GROUP_EPS):
     """Per-token group quant: (q e4m3 [M, K], scale fp32 [M, K/group]) row-major."""
     M, K = x.shape
     xf = x.float().reshape(M, K // group, group)
-    amax = torch.clamp(xf.abs().amax(dim=-1), min=torch.tensor(eps, dtype=torch.float32))
-    inv = torch.tensor(1.0 / FP8_MAX, dtype=torch.float32)
-    s = amax * inv
+    amax = torch.clamp_min(xf.abs().amax(dim=-1), eps)
+    s = amax * torch.full_like(amax, 1.0 / FP8_MAX)          # amax * fp32(1/448)
     q = (xf / s.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(FP8).reshape(M, K)
     return q, s.contiguous()
 

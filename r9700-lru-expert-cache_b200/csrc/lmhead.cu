@@ -263,6 +263,54 @@ __device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32
   }
 }
 
+// ---- row statistics: CTA partial per token, then the last CTA to finish merges them ---------
+// red[w * stride + m] holds warp w's state for token m (nred warps). Call with every thread
+// of the CTA after a barrier that published `red`. The workspace partials are token-major
+// ([m][cta]) so the final merge reads them coalesced; the last CTA resets the ticket.
+__device__ void stats_finalize(const Params& p, const b200::RowStat* red, int stride, int nred,
+                               int* s_flag) {
+  const int G = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  if (threadIdx.x < p.M) {
+    const int m = threadIdx.x;
+    b200::RowStat r = red[m];
+    for (int w = 1; w < nred; ++w) r = b200::rowstat_merge(r, red[w * stride + m]);
+    float* dst = p.partial + ((long long)m * G + blockIdx.x) * 3;
+    dst[0] = r.m;
+    dst[1] = __int_as_float(r.idx);
+    dst[2] = r.s;
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned ticket = atomicAdd(p.counter, 1u);
+    *s_flag = (ticket == (unsigned)G - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (*s_flag == 0) return;
+  __threadfence();
+  for (int m = warp; m < p.M; m += nwarps) {
+    b200::RowStat r;
+    b200::rowstat_init(r);
+    for (int c = lane; c < G; c += 32) {
+      const float* src = p.partial + ((long long)m * G + c) * 3;
+      b200::RowStat o;
+      o.m = __ldcg(src);
+      o.idx = __float_as_int(__ldcg(src + 1));
+      o.s = __ldcg(src + 2);
+      r = b200::rowstat_merge(r, o);
+    }
+#pragma unroll
+    for (int msk = 1; msk < 32; msk <<= 1) r = b200::rowstat_merge(r, b200::rowstat_shfl_xor(r, msk));
+    if (lane == 0) {
+      if (p.row_max) p.row_max[m] = r.m;
+      if (p.row_arg) p.row_arg[m] = r.idx;
+      if (p.row_lse) p.row_lse[m] = r.m + logf(r.s);
+    }
+  }
+  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
+}
+
 // ---- the kernel ------------------------------------------------------------------------------
 
 template <int KIND, int NT8, bool STATS>
@@ -415,46 +463,339 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
 
   if (!STATS) return;
   __syncthreads();
-  // ---- CTA partial per token, then the last CTA to finish merges all partials ------------
-  const int G = gridDim.x;
-  if (threadIdx.x < p.M) {
-    const int m = threadIdx.x;
-    b200::RowStat r = red[m];
-    for (int w = 1; w < NC; ++w) r = b200::rowstat_merge(r, red[w * MAXM + m]);
-    float* dst = p.partial + ((long long)m * G + blockIdx.x) * 3;
-    dst[0] = r.m;
-    dst[1] = __int_as_float(r.idx);
-    dst[2] = r.s;
-    __threadfence();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned ticket = atomicAdd(p.counter, 1u);
-    *s_flag = (ticket == (unsigned)G - 1) ? 1 : 0;
-  }
-  __syncthreads();
-  if (*s_flag == 0) return;
-  __threadfence();
-  for (int m = warp; m < p.M; m += NC + 1) {
-    b200::RowStat r;
-    b200::rowstat_init(r);
-    for (int c = lane; c < G; c += 32) {
-      const float* src = p.partial + ((long long)m * G + c) * 3;
-      b200::RowStat o;
-      o.m = __ldcg(src);
-      o.idx = __float_as_int(__ldcg(src + 1));
-      o.s = __ldcg(src + 2);
-      r = b200::rowstat_merge(r, o);
-    }
+  stats_finalize(p, red, MAXM, NC, s_flag);
+}
+
+// ---- tcgen05 path: 16 < M <= 64 tokens ---------------------------------------------------------
+//
+// At these row counts the GEMV's warp MMAs would issue-bound the SM, so the contraction moves
+// to the 5th-generation tensor core: D[128 weight rows, T tokens] (fp32, in TMEM) = W tile
+// (A, 128 x 128 K, shared memory) x X tile (B, T x 128 K). A 128x128 weight tile is exactly one
+// block-scale block, so every tile gets its own TMEM accumulator and the two scales are applied
+// in fp32 when the epilogue reads it back:  y[n, t] += ws[n/128, kb] * xs[t, kb] * D_kb[n, t].
+//   warp 0 (1 lane): bulk-async copies of each stage = 8 strip chunks of 2 KB (the 128-row
+//                    tile, landing in the 128-byte-swizzled K-major layout the descriptor names)
+//                    + the activation tile of that 128-K block (T x 128 B, pre-tiled);
+//   warp 1 (1 lane): TMEM allocation, then 4 tcgen05.mma kind::f8f6f4 (K = 32 each) per stage,
+//                    committed to the stage's empty barrier and the accumulator's full barrier;
+//   warps 2-5      : tcgen05.ld of their 32 TMEM lanes, fp32 scale-accumulate, and per 128-row
+//                    block the bf16 logits and the (max, argmax, sum exp) update.
+// TMEM holds 512 / T accumulators, so the MMA warp runs ahead of the epilogue by that many
+// 128-K blocks. The activation is quantized once per call by act_tiles_kernel into the
+// workspace, already swizzled, so every stage fetches it with one copy from L2.
+
+constexpr int TC_THREADS = 192;
+constexpr int TC_MAX_STAGES = 8;
+constexpr int TC_MAX_BUF = 16;
+constexpr int TC_TILE_W = 128 * 128;
+constexpr int TC_HDR = 512;                         // barriers, TMEM slot, flag
+constexpr int TC_RED = 4 * 64 * 12;                 // [4 warps][64 tokens] RowStat
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);      // start address, bits [0,14)
+  d |= (uint64_t)1 << 16;                                // leading byte offset (unused here)
+  d |= (uint64_t)(1024 >> 4) << 32;                      // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                                // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                                // layout: SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void tc_mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   b200::smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
 #pragma unroll
-    for (int msk = 1; msk < 32; msk <<= 1) r = b200::rowstat_merge(r, b200::rowstat_shfl_xor(r, msk));
-    if (lane == 0) {
-      if (p.row_max) p.row_max[m] = r.m;
-      if (p.row_arg) p.row_arg[m] = r.idx;
-      if (p.row_lse) p.row_lse[m] = r.m + logf(r.s);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int TPAD>
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[TPAD]) {
+  float a[32];
+  tmem_ld32(taddr, a);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = a[i];
+  if constexpr (TPAD == 64) {
+    float b[32];
+    tmem_ld32(taddr + 32, b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[32 + i] = b[i];
+  }
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// x (bf16 [M, K]) -> per-token group-128 quant, written as tiles qt[kb][tpad rows][128 B] in the
+// 128-byte-swizzled layout (rows >= M zero) + scales xt[kb][tpad]; with qx_in set, re-tile an
+// already quantized e4m3 [M, K] + xs [M, K/128] instead. Same formula as the standalone quant.
+// grid = (K/128, tpad/8), 128 threads: half a warp per (row, 128-K block).
+__global__ void __launch_bounds__(128)
+    act_tiles_kernel(const __nv_bfloat16* __restrict__ x, const uint8_t* __restrict__ qx_in,
+                     const float* __restrict__ xs_in, int M, int K, int tpad,
+                     uint8_t* __restrict__ qt, float* __restrict__ xt, uint8_t* __restrict__ qx_out,
+                     float* __restrict__ xs_out) {
+  const int KB = K / 128, kb = blockIdx.x;
+  const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+  const unsigned hmask = 0xffffu << (16 * (hw & 1));
+  const int m = blockIdx.y * 8 + hw;
+  uint2 b = make_uint2(0, 0);
+  float sc = 0.f;
+  if (m < M) {
+    if (qx_in != nullptr) {
+      b = *reinterpret_cast<const uint2*>(qx_in + (long long)m * K + kb * 128 + hl * 8);
+      sc = xs_in[m * KB + kb];
+    } else {
+      const uint4 r = *reinterpret_cast<const uint4*>(x + (long long)m * K + kb * 128 + hl * 8);
+      const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
+      float f[8];
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        f[i] = __bfloat162float(rv[i]);
+        amax = fmaxf(amax, fabsf(f[i]));
+      }
+#pragma unroll
+      for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
+      sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+      b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
+                             fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
+      b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
+                             fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+      if (qx_out != nullptr) {
+        *reinterpret_cast<uint2*>(qx_out + (long long)m * K + kb * 128 + hl * 8) = b;
+        if (hl == 0) xs_out[m * KB + kb] = sc;
+      }
     }
   }
-  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
+  if (m < tpad) {
+    uint8_t* tile = qt + ((long long)kb * tpad + m) * 128;
+    *reinterpret_cast<uint2*>(tile + (((hl >> 1) ^ (m & 7)) * 16) + (hl & 1) * 8) = b;
+    if (hl == 0) xt[kb * tpad + m] = sc;
+  }
+}
+
+template <int TPAD, bool STATS>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    fp8_tc_kernel(Params p, const uint8_t* __restrict__ qt, const float* __restrict__ xt) {
+  extern __shared__ char sm_raw[];
+  const uint32_t raw = b200::smem_u32(sm_raw);
+  char* sm = sm_raw + ((1024u - (raw & 1023u)) & 1023u);
+  constexpr int XT_BYTES = TPAD * 128;
+  constexpr int STAGE = TC_TILE_W + XT_BYTES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = p.K / 128;
+  const int nblk = p.N / 128;
+  const int b0 = (int)(((long long)blockIdx.x * nblk) / gridDim.x);
+  const int b1 = (int)(((long long)(blockIdx.x + 1) * nblk) / gridDim.x);
+  const int total = (b1 - b0) * KB;
+  const int nstage = p.nstage, nbuf = p.kps;          // kps carries the accumulator count here
+
+  uint64_t* w_full = reinterpret_cast<uint64_t*>(sm);
+  uint64_t* w_empty = w_full + TC_MAX_STAGES;
+  uint64_t* a_full = w_empty + TC_MAX_STAGES;
+  uint64_t* a_empty = a_full + TC_MAX_BUF;
+  uint64_t* xs_bar = a_empty + TC_MAX_BUF;
+  uint64_t* done_bar = xs_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + TC_HDR);
+  float* xs_s = reinterpret_cast<float*>(sm + p.xs_off);       // [KB][TPAD]
+  char* ring = sm + p.ring_off;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nstage; ++i) {
+      b200::mbar_init(&w_full[i], 1);
+      b200::mbar_init(&w_empty[i], 1);
+    }
+    for (int i = 0; i < nbuf; ++i) {
+      b200::mbar_init(&a_full[i], 1);
+      b200::mbar_init(&a_empty[i], 4);
+    }
+    b200::mbar_init(xs_bar, 1);
+    b200::mbar_init(done_bar, 1);
+    b200::fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     b200::smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint64_t deadline = b200::globaltimer_ns() + WAIT_NS;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = b200::l2_policy_evict_first();
+      b200::mbar_arrive_expect_tx(xs_bar, TPAD * KB * 4);
+      b200::bulk_g2s(xs_s, xt, TPAD * KB * 4, xs_bar);
+      int issued = 0;
+      bool ok = true;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % nstage, round = it / nstage;
+        if (round > 0 && !b200::mbar_wait_bounded(&w_empty[s], (round - 1) & 1, deadline)) {
+          ok = false;
+          break;
+        }
+        const int blk = b0 + it / KB, kb = it % KB;
+        char* st = ring + s * STAGE;
+        b200::mbar_arrive_expect_tx(&w_full[s], STAGE);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          b200::bulk_g2s_stream(st + j * FP8_KB_BYTES,
+                                p.w + ((long long)(blk * 8 + j) * KB + kb) * FP8_KB_BYTES,
+                                FP8_KB_BYTES, &w_full[s], pol);
+        b200::bulk_g2s(st + TC_TILE_W, qt + (long long)kb * XT_BYTES, XT_BYTES, &w_full[s]);
+        ++issued;
+      }
+      if (!ok) atomicExch(&g_lmhead_err, 1);
+      for (int q = max(0, issued - nstage); q < issued; ++q)
+        b200::mbar_wait_bounded(&w_full[q % nstage], (q / nstage) & 1, deadline + WAIT_NS);
+      b200::mbar_wait_bounded(xs_bar, 0, deadline + WAIT_NS);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4)                        // D: f32
+                             | ((uint32_t)(TPAD >> 3) << 17)  // N
+                             | ((uint32_t)(128 >> 4) << 24);  // M = 128; A, B e4m3, K-major
+      bool ok = true;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % nstage, buf = it % nbuf;
+        if (!b200::mbar_wait_bounded(&w_full[s], (it / nstage) & 1, deadline)) { ok = false; break; }
+        if (it >= nbuf && !b200::mbar_wait_bounded(&a_empty[buf], ((it / nbuf) - 1) & 1, deadline)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = b200::smem_u32(ring + s * STAGE);
+        const uint64_t ad = sw128_desc(st), bd = sw128_desc(st + TC_TILE_W);
+        const uint32_t d = tmem + (uint32_t)(buf * TPAD);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc_mma_f8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
+        tc_commit(&w_empty[s]);
+        tc_commit(&a_full[buf]);
+      }
+      if (!ok) atomicExch(&g_lmhead_err, 1);
+      tc_commit(done_bar);                                     // every issued MMA has landed
+      b200::mbar_wait_bounded(done_bar, 0, deadline + WAIT_NS);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int qd = warp & 3;                  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    b200::RowStat st[TPAD / 32];
+#pragma unroll
+    for (int i = 0; i < TPAD / 32; ++i) b200::rowstat_init(st[i]);
+    bool ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xs_bar, 0, deadline));
+    int it = 0;
+    for (int blk = b0; blk < b1 && ok; ++blk) {
+      float acc[TPAD];
+#pragma unroll
+      for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
+      const float* wsrow = static_cast<const float*>(p.wscale) + (long long)blk * KB;
+      const float wsv = (lane < KB) ? __ldg(wsrow + lane) : 0.f;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int buf = it % nbuf;
+        const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb) : __ldg(wsrow + kb);
+        if (!__all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (it / nbuf) & 1, deadline))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
+        float v[TPAD];
+        tmem_ld_row<TPAD>(ta, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
+        const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
+#pragma unroll
+        for (int j = 0; j < TPAD; j += 4) {
+          const float4 xv = xs4[j >> 2];
+          acc[j] = fmaf(v[j], sw * xv.x, acc[j]);
+          acc[j + 1] = fmaf(v[j + 1], sw * xv.y, acc[j + 1]);
+          acc[j + 2] = fmaf(v[j + 2], sw * xv.z, acc[j + 2]);
+          acc[j + 3] = fmaf(v[j + 3], sw * xv.w, acc[j + 3]);
+        }
+      }
+      if (!ok) break;
+      const int n = blk * 128 + 32 * qd + lane;
+      if (p.y != nullptr) {
+#pragma unroll
+        for (int j = 0; j < TPAD; ++j)
+          if (j < p.M) p.y[(long long)j * p.ldy + n] = __float2bfloat16_rn(acc[j]);
+      }
+      if (STATS) {
+        const int base = (int)(blk * 128 + 32 * qd + p.vocab_offset);
+#pragma unroll
+        for (int j = 0; j < TPAD; ++j) {
+          if (j < p.M) {
+            const float v = acc[j];
+            const float wm = b200::warp_max(v);
+            const unsigned bal = __ballot_sync(0xffffffffu, v == wm);
+            const float es = b200::warp_sum(expf(v - wm));
+            if (lane == (j & 31)) {
+              b200::RowStat o;
+              o.m = wm;
+              o.idx = base + __ffs(bal) - 1;
+              o.s = es;
+              st[j >> 5] = b200::rowstat_merge(st[j >> 5], o);
+            }
+          }
+        }
+      }
+    }
+    if (!ok) atomicExch(&g_lmhead_err, 1);
+    if (STATS) {
+#pragma unroll
+      for (int i = 0; i < TPAD / 32; ++i) red[ew * 64 + 32 * i + lane] = st[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+  if (STATS) stats_finalize(p, red, 64, 4, s_flag);
 }
 
 // ---- read-only stream control (hcq_stream_probe, hcq_fp8skinny.hip:206-224) -----------------
@@ -528,16 +869,66 @@ int launch_m(const Params& p, cudaStream_t stream) {
   return (p.M <= 8) ? launch_one<KIND, 1, STATS>(p, stream) : launch_one<KIND, 2, STATS>(p, stream);
 }
 
-constexpr long long WORKSPACE_BYTES = 16 + 1024LL * MAXM * 12;
+// Workspace: [0,16) ticket counter | [16, 16+1024*64*12) per-CTA row statistics |
+// [QT_OFF, +QT_CAP) swizzled activation tiles | [XT_OFF, +XT_CAP) their scales.
+constexpr long long PART_CAP = 1024LL * 64 * 12;
+constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
+constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
+constexpr long long WORKSPACE_BYTES = XT_OFF + XT_CAP;
+static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
 
-// Runs M in chunks of 16 tokens (one weight pass each).
+int plan_tc(Params& p, int tpad) {
+  const int KB = p.K / 128;
+  p.xs_off = TC_HDR + TC_RED;
+  p.ring_off = (p.xs_off + tpad * KB * 4 + 1023) & ~1023;
+  const int stage = TC_TILE_W + tpad * 128;
+  const int avail = SMEM_CAP - 1024 - p.ring_off;
+  const int nstage = min(TC_MAX_STAGES, avail / stage);
+  if (nstage < 2) return -1;
+  p.nstage = nstage;
+  p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
+  return 1024 + p.ring_off + nstage * stage;
+}
+
+template <int TPAD, bool STATS>
+int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t stream) {
+  const int KB = p.K / 128;
+  if ((long long)KB * TPAD * 128 > QT_CAP || (long long)TPAD * KB * 4 > XT_CAP) return -8;
+  char* base = reinterpret_cast<char*>(p.counter);
+  uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
+  float* xt = reinterpret_cast<float*>(base + XT_OFF);
+  act_tiles_kernel<<<dim3(KB, TPAD / 8), 128, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M, p.K, TPAD, qt,
+      xt, p.qx_out, p.xs_out);
+  const int smem = plan_tc(p, TPAD);
+  if (smem < 0) return -8;
+  auto kern = fp8_tc_kernel<TPAD, STATS>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  const int grid = min(p.N / 128, num_sms());
+  kern<<<grid, TC_THREADS, smem, stream>>>(p, qt, xt);
+  return (int)cudaGetLastError();
+}
+
+template <bool STATS>
+int launch_tc(const Params& p, const uint8_t* qx_in, const float* xs_in, cudaStream_t stream) {
+  return (p.M <= 32) ? launch_tc_t<32, STATS>(p, qx_in, xs_in, stream)
+                     : launch_tc_t<64, STATS>(p, qx_in, xs_in, stream);
+}
+
+// Runs M in token chunks, one weight pass each: FP8 with a workspace takes 64-token chunks and
+// sends every chunk above 16 tokens to the tcgen05 kernel; everything else goes through the
+// 16-token GEMV.
 template <int KIND>
 int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
   const int M = p.M, KB = p.K / 128;
   const bool stats = (p.row_max || p.row_arg || p.row_lse);
-  for (int m0 = 0; m0 < M; m0 += MAXM) {
+  const bool tc_ok = (KIND == FP8_QUANT || KIND == FP8_PREQ) && p.counter != nullptr &&
+                     (long long)KB * 64 * 128 <= QT_CAP;
+  const int chunk = tc_ok ? 64 : MAXM;
+  for (int m0 = 0; m0 < M; m0 += chunk) {
     Params q = p;
-    q.M = min(MAXM, M - m0);
+    q.M = min(chunk, M - m0);
     q.x = static_cast<const char*>(p.x) + (long long)m0 * p.K * x_elem_bytes;
     if (p.xs_in) q.xs_in = p.xs_in + (long long)m0 * KB;
     if (p.y) q.y = p.y + (long long)m0 * p.ldy;
@@ -546,7 +937,13 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
     if (p.row_lse) q.row_lse = p.row_lse + m0;
     if (p.qx_out) q.qx_out = p.qx_out + (long long)m0 * p.K;
     if (p.xs_out) q.xs_out = p.xs_out + (long long)m0 * KB;
-    const int rc = stats ? launch_m<KIND, true>(q, stream) : launch_m<KIND, false>(q, stream);
+    int rc;
+    if (tc_ok && q.M > MAXM) {
+      const uint8_t* qx_in = (KIND == FP8_PREQ) ? static_cast<const uint8_t*>(q.x) : nullptr;
+      rc = stats ? launch_tc<true>(q, qx_in, q.xs_in, stream) : launch_tc<false>(q, qx_in, q.xs_in, stream);
+    } else {
+      rc = stats ? launch_m<KIND, true>(q, stream) : launch_m<KIND, false>(q, stream);
+    }
     if (rc != 0) return rc;
   }
   return 0;

@@ -128,9 +128,10 @@ def gemm_fp8_block(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor) -> torch
     _check(x, wq, ws)
     M, K = x.shape
     y = torch.empty(M, wq.shape[0], dtype=torch.bfloat16, device=x.device)
+    wsp = workspace(x.device)
     rc = _lib.lmhead().b200_fp8_lmhead(
         _lib.ptr(x), M, K, _lib.ptr(wq), _lib.ptr(ws), wq.shape[0], 0, _lib.ptr(y), y.stride(0),
-        None, None, None, None, None, None, 0, _lib.stream_ptr())
+        None, None, None, None, None, _lib.ptr(wsp), wsp.numel(), _lib.stream_ptr())
     _lib.check(rc, "b200_fp8_lmhead")
     return y
 
