@@ -295,6 +295,57 @@ def probe_ceiling(P, dev, nbytes: int) -> float:
 # main
 # ---------------------------------------------------------------------------------------
 
+def run_op(args):
+    """One op alone, eager launches (what ncu captures): --op fp8|w4|lru|silu."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    P = load_pkg()
+    res = {"op": args.op}
+    if args.op in ("fp8", "w4"):
+        n = args.rows
+        x = torch.randn(args.m, K_HID, device=dev, dtype=torch.bfloat16)
+        if args.op == "fp8":
+            w = (torch.randn(n, K_HID, device=dev) * 0.02).bfloat16()
+            wq, ws = P.fp8_target_lmhead.pack_fp8_block(w)
+            del w
+            fn = lambda: P.fp8_target_lmhead.fp8_lmhead(x, wq, ws)
+            nbytes = fp8_bytes(n, K_HID, args.m)
+        else:
+            w = (torch.randn(n, K_HID, device=dev) * 0.02).bfloat16()
+            pk = P.draft_w4_lmhead.pack_w4a16(w)
+            del w
+            fn = lambda: P.draft_w4_lmhead.gemm_w4a16_top(x, pk)
+            nbytes = w4_bytes(pk.n_pad, K_HID, args.m)
+    elif args.op == "silu":
+        x = torch.randn(8, 1024, device=dev, dtype=torch.bfloat16)
+        fn = lambda: P.fused_silu_mul_quant.silu_mul_quant(x, torch.float8_e4m3fn)
+        nbytes = 20512
+    elif args.op == "lru":
+        from oracle import lru_oracle as LO
+        rng = np.random.default_rng(0)
+        hot = sorted(rng.choice(E_EXPERTS, S_SLOTS, replace=False).tolist())
+        lay = P.lru.LruLayer.warm(hot, E_EXPERTS, dev, stamps=torch.as_tensor(rng.permutation(S_SLOTS) + 1),
+                                  step=S_SLOTS, max_inserts=64)
+        ids = torch.as_tensor(LO.zipf_rows(rng, E_EXPERTS, 5, TOPK).ravel().astype(np.int32), device=dev)
+        out = lay.new_align_outputs(ids.numel())
+        fn = lambda: lay.fused(ids, out)
+        nbytes = 0
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    res.update({"us_per_call_eager": us, "m": args.m, "rows": args.rows,
+                "GB_s": (nbytes / us / 1e3) if nbytes else None,
+                "lmhead_error": int(P._lib.lmhead().b200_lmhead_error(0))})
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,7 +353,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the secondary measurements")
+    ap.add_argument("--op", choices=["fp8", "w4", "lru", "silu"], default=None,
+                    help="time one op alone with eager launches (for profiling)")
+    ap.add_argument("--m", type=int, default=M_ROWS)
+    ap.add_argument("--rows", type=int, default=N_VOCAB)
     args = ap.parse_args()
+    if args.op is not None:
+        return run_op(args)
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -326,7 +383,7 @@ def main():
     torch.manual_seed(0)
     x = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
     y = torch.empty(M_ROWS, n_loc, dtype=torch.bfloat16, device=dev)
-    launches_per_step = math.ceil(M_ROWS / 16)
+    launches_per_step = 2 * math.ceil(M_ROWS / 64)      # activation tiles + tcgen05 GEMM
 
     def step(i, kev=None):
         wq, ws = pool[i % len(pool)]
@@ -437,7 +494,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                          "peak_source": pk["source"], "kernel_us": kern_us_max,
-                         "kernel": "gemv_kernel<FP8_QUANT> x" + str(launches_per_step),
+                         "kernel": "act_tiles_kernel + fp8_tc_kernel<64> (tcgen05)",
                          "bytes_per_launch_set": per_launch_bytes,
                          "read_control_GB_s": ceiling},
             "cpu_baseline": cpu,

@@ -32,16 +32,20 @@
 //           k = 128kb + 32w + 8t + j, code j in nibble (j&1)*4 + (j>>1), offset binary.
 //   W4  wsz: int32 [N/16, K/128, 16] = f16 scale | f16(-(1024 + zero)) << 16
 //           (draft_w4_lmhead.py:47-48, unchanged).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr int NC = 4;                    // consumer warps
-constexpr int NTHREADS = 32 * (NC + 1);
-constexpr int MAXM = 16;                 // tokens per launch
+constexpr int NC_FP8 = 4;                // consumer warps of the FP8 GEMV
+constexpr int NC_W4 = 8;                 // consumer warps of the W4 GEMV (more ALU per byte)
+constexpr int MAXM = 16;                 // tokens per GEMV launch
 constexpr int SMEM_CAP = 227 * 1024;
 constexpr int MAX_STAGES = 8;
 constexpr int FP8_KB_BYTES = 16 * 128;   // one strip x one 128-K block
@@ -69,15 +73,24 @@ struct Params {
   float* xs_out;
   unsigned* counter;
   float* partial;
-  int kps;           // 128-K blocks per stage
+  int kps;           // 128-K blocks per stage (tcgen05 path: TMEM accumulators)
   int nstage;
   int stage_bytes;
   int xs_stride;     // bytes per activation row in shared memory
   int x_off, xs_off, ring_off;
+  int pdl;           // 1: launched as the programmatic dependent of the activation kernel
 };
 
+template <int NC>
 __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
+}
+
+// Programmatic dependent launch: the dependent grid may start while its primary still runs;
+// griddep_wait() blocks until the primary grid has completed and its writes are visible.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -99,17 +112,24 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
 }
 
 // ---- activation prologue -----------------------------------------------------------------
-
-// FP8: quantize x (bf16 [M, K]) per token group of 128 into shared memory; rows >= M zero.
-// Same formula as b200_per_token_group_quant_fp8 (bit-identical): s = max(amax,1e-10)*(1/448).
-template <int KIND>
-__device__ void load_activation(const Params& p, char* sm, int rows_x) {
-  const int ctid = threadIdx.x - 32;            // consumer thread 0..127
+//
+// FP8_QUANT: quantize x (bf16 [M, K]) per token group of 128 straight into shared memory
+//   (bit-identical to b200_per_token_group_quant_fp8: s = max(amax, 1e-10) * (1/448)); used
+//   when the caller gives no workspace.
+// FP8_PREQ: e4m3 rows [M, K] (+ fp32 scales [M, K/128]) arrive by one bulk copy per row; with
+//   p.pdl they were written by act_rows_kernel, this kernel's programmatic primary.
+// W4_*: the raw activation rows arrive by one bulk copy per row and bf16 is rounded to f16 in
+//   shared memory (round to nearest even, i.e. x.to(float16)).
+// Rows >= M are zero (and their scales 0), so they add nothing to any accumulator.
+template <int KIND, int NC>
+__device__ void load_activation(const Params& p, char* sm, int rows_x, uint64_t* x_bar,
+                                uint64_t deadline, bool* ok) {
+  const int ctid = threadIdx.x - 32;            // consumer thread 0..NC*32-1
   const int KB = p.K / 128;
   uint8_t* X = reinterpret_cast<uint8_t*>(sm + p.x_off);
   float* xs = reinterpret_cast<float*>(sm + p.xs_off);
   if (KIND == FP8_QUANT) {
-    const int half = ctid >> 4, hl = ctid & 15;  // 8 half-warps, 16 lanes x 8 elements
+    const int half = ctid >> 4, hl = ctid & 15;  // half-warps, 16 lanes x 8 elements
     const unsigned hmask = 0xffffu << (16 * ((ctid >> 4) & 1));
     const int ngroups = rows_x * KB;
     for (int gi = half; gi < ngroups; gi += NC * 2) {
@@ -145,37 +165,37 @@ __device__ void load_activation(const Params& p, char* sm, int rows_x) {
         if (hl == 0) p.xs_out[m * KB + kb] = sc;
       }
     }
-  } else if (KIND == FP8_PREQ) {
-    const int nvec = rows_x * (p.K / 16);
-    for (int i = ctid; i < nvec; i += NC * 32) {
-      const int m = i / (p.K / 16), c = i % (p.K / 16);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m < p.M) v = *(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) + (long long)m * p.K) + c);
-      *reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16) = v;
-    }
-    for (int i = ctid; i < rows_x * KB; i += NC * 32) {
-      const int m = i / KB;
-      xs[i] = (m < p.M) ? p.xs_in[i] : 0.f;
-    }
-  } else {
-    // W4: f16 activation rows (bf16 input converted with round-to-nearest-even == x.to(f16))
-    const int nvec = rows_x * (p.K / 8);
-    for (int i = ctid; i < nvec; i += NC * 32) {
+    return;
+  }
+  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  const int row_bytes = IS_W4 ? 2 * p.K : p.K;
+  if (p.pdl) griddep_wait();
+  if (ctid == 0) {
+    b200::mbar_arrive_expect_tx(x_bar, (uint32_t)(p.M * row_bytes));
+    for (int m = 0; m < p.M; ++m)
+      b200::bulk_g2s(X + m * p.xs_stride, static_cast<const uint8_t*>(p.x) + (long long)m * row_bytes,
+                     row_bytes, x_bar);
+  }
+  // zero rows >= M while the copies fly; scales straight from global memory
+  for (int i = ctid; i < (rows_x - p.M) * (row_bytes / 16); i += NC * 32) {
+    const int m = p.M + i / (row_bytes / 16), c = i % (row_bytes / 16);
+    *reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16) = make_uint4(0, 0, 0, 0);
+  }
+  if (!IS_W4)
+    for (int i = ctid; i < rows_x * KB; i += NC * 32) xs[i] = (i / KB < p.M) ? p.xs_in[i] : 0.f;
+  *ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(x_bar, 0, deadline));
+  if (KIND == W4_BF16) {
+    consumer_bar<NC>();                           // (every consumer warp reaches it)
+    if (!*ok) return;
+    for (int i = ctid; i < p.M * (p.K / 8); i += NC * 32) {
       const int m = i / (p.K / 8), c = i % (p.K / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m < p.M) {
-        const uint4 r = *(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + (long long)m * p.K) + c);
-        if (KIND == W4_BF16) {
-          const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
-          __half h[8];
+      uint4* q = reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16);
+      const uint4 r = *q;
+      const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
+      __half h[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(rv[j]));
-          v = *reinterpret_cast<const uint4*>(h);
-        } else {
-          v = r;
-        }
-      }
-      *reinterpret_cast<uint4*>(X + m * p.xs_stride + c * 16) = v;
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(rv[j]));
+      *q = *reinterpret_cast<const uint4*>(h);
     }
   }
 }
@@ -313,8 +333,13 @@ __device__ void stats_finalize(const Params& p, const b200::RowStat* red, int st
 
 // ---- the kernel ------------------------------------------------------------------------------
 
-template <int KIND, int NT8, bool STATS>
-__global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
+// Shared-memory header of the GEMV: full/empty barriers [0, 128), the activation barrier at
+// 128, per-warp row statistics from 256, the "last CTA" flag after them.
+constexpr int GEMV_HDR_RED = 256;
+__host__ __device__ constexpr int gemv_hdr(int nc) { return GEMV_HDR_RED + nc * MAXM * 12 + 16; }
+
+template <int KIND, int NT8, bool STATS, int NC>
+__global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   extern __shared__ __align__(128) char sm[];
   constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
   constexpr int KB_BYTES = IS_W4 ? W4_KB_BYTES : FP8_KB_BYTES;
@@ -328,8 +353,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
 
   uint64_t* full = reinterpret_cast<uint64_t*>(sm);
   uint64_t* empty = full + MAX_STAGES;
-  b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + 128);   // [NC][MAXM]
-  int* s_flag = reinterpret_cast<int*>(sm + 128 + NC * MAXM * sizeof(b200::RowStat));
+  uint64_t* x_bar = reinterpret_cast<uint64_t*>(sm + 128);
+  b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + GEMV_HDR_RED);   // [NC][MAXM]
+  int* s_flag = reinterpret_cast<int*>(sm + GEMV_HDR_RED + NC * MAXM * sizeof(b200::RowStat));
   char* ring = sm + p.ring_off;
 
   if (threadIdx.x == 0) {
@@ -337,6 +363,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
       b200::mbar_init(&full[i], 1);
       b200::mbar_init(&empty[i], 1);
     }
+    b200::mbar_init(x_bar, 1);
     b200::fence_mbar_init();
   }
   __syncthreads();
@@ -383,13 +410,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(Params p) {
   } else {
     // ---------------- consumers ----------------
     const int cw = warp - 1;
-    load_activation<KIND>(p, sm, 8 * NT8);
-    consumer_bar();
+    bool ok = true;
+    load_activation<KIND, NC>(p, sm, 8 * NT8, x_bar, deadline, &ok);
+    consumer_bar<NC>();
+    ok = ok && __all_sync(0xffffffffu, ok);
     const uint32_t xbase = b200::smem_u32(sm + p.x_off);
     const float* xs = reinterpret_cast<const float*>(sm + p.xs_off);
     const uint32_t ring_u32 = b200::smem_u32(ring);
     const int g = lane >> 2, t = lane & 3;
-    bool ok = true;
     for (int ls = cw; ls < s1 - s0 && ok; ls += NC) {
       const int strip = s0 + ls;
       float tot[NT8][4];
@@ -564,6 +592,7 @@ __global__ void __launch_bounds__(128)
                      const float* __restrict__ xs_in, int M, int K, int tpad,
                      uint8_t* __restrict__ qt, float* __restrict__ xt, uint8_t* __restrict__ qx_out,
                      float* __restrict__ xs_out) {
+  griddep_launch_dependents();              // the GEMM may start streaming weights now
   const int KB = K / 128, kb = blockIdx.x;
   const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
   const unsigned hmask = 0xffffu << (16 * (hw & 1));
@@ -604,9 +633,43 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// x (bf16 [M, K]) -> e4m3 rows qr [M, K] + fp32 scales sr [M, K/128] (row-major, the
+// per_token_group_quant_fp8 layout): the programmatic primary of the FP8 GEMV, which pulls the
+// rows with one bulk copy each. grid = (K/128, ceil(M/8)), half a warp per (row, 128-K block).
+__global__ void __launch_bounds__(128)
+    act_rows_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, uint8_t* __restrict__ qr,
+                    float* __restrict__ sr) {
+  griddep_launch_dependents();
+  const int KB = K / 128, kb = blockIdx.x;
+  const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+  const unsigned hmask = 0xffffu << (16 * (hw & 1));
+  const int m = blockIdx.y * 8 + hw;
+  if (m >= M) return;                        // a whole half-warp leaves together
+  const uint4 r = *reinterpret_cast<const uint4*>(x + (long long)m * K + kb * 128 + hl * 8);
+  const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(&r);
+  float f[8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    f[i] = __bfloat162float(rv[i]);
+    amax = fmaxf(amax, fabsf(f[i]));
+  }
+#pragma unroll
+  for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
+  const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
+  uint2 b;
+  b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
+                         fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
+  b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
+                         fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+  *reinterpret_cast<uint2*>(qr + (long long)m * K + kb * 128 + hl * 8) = b;
+  if (hl == 0) sr[m * KB + kb] = sc;
+}
+
 template <int TPAD, bool STATS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    fp8_tc_kernel(Params p, const uint8_t* __restrict__ qt, const float* __restrict__ xt) {
+    fp8_tc_kernel(const __grid_constant__ CUtensorMap wmap, Params p, const uint8_t* __restrict__ qt,
+                  const float* __restrict__ xt) {
   extern __shared__ char sm_raw[];
   const uint32_t raw = b200::smem_u32(sm_raw);
   char* sm = sm_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -659,27 +722,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 0) {
     // ---------------- producer ----------------
+    // Weight tiles do not depend on the activation kernel (this grid's programmatic primary),
+    // so the first ring of weight tiles is issued before griddepcontrol.wait; each stage's
+    // activation tile (and the scales) only after it.
     if (lane == 0) {
       const uint64_t pol = b200::l2_policy_evict_first();
+      const uint64_t wmap_addr = reinterpret_cast<uint64_t>(&wmap);
+      auto issue_w = [&](int it) {
+        const int s = it % nstage;
+        const int blk = b0 + it / KB, kb = it % KB;
+        b200::mbar_arrive_expect_tx(&w_full[s], STAGE);
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+            " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(b200::smem_u32(ring + s * STAGE)),
+            "l"(wmap_addr), "r"(0), "r"(0), "r"(kb), "r"(blk * 8), "r"(b200::smem_u32(&w_full[s])),
+            "l"(pol)
+            : "memory");
+      };
+      auto issue_x = [&](int it) {
+        const int s = it % nstage, kb = it % KB;
+        b200::bulk_g2s(ring + s * STAGE + TC_TILE_W, qt + (long long)kb * XT_BYTES, XT_BYTES, &w_full[s]);
+      };
+      const int first = min(nstage, total);
+      for (int it = 0; it < first; ++it) issue_w(it);
+      if (p.pdl) griddep_wait();
       b200::mbar_arrive_expect_tx(xs_bar, TPAD * KB * 4);
       b200::bulk_g2s(xs_s, xt, TPAD * KB * 4, xs_bar);
-      int issued = 0;
+      for (int it = 0; it < first; ++it) issue_x(it);
+      int issued = first;
       bool ok = true;
-      for (int it = 0; it < total; ++it) {
+      for (int it = first; it < total; ++it) {
         const int s = it % nstage, round = it / nstage;
-        if (round > 0 && !b200::mbar_wait_bounded(&w_empty[s], (round - 1) & 1, deadline)) {
+        if (!b200::mbar_wait_bounded(&w_empty[s], (round - 1) & 1, deadline)) {
           ok = false;
           break;
         }
-        const int blk = b0 + it / KB, kb = it % KB;
-        char* st = ring + s * STAGE;
-        b200::mbar_arrive_expect_tx(&w_full[s], STAGE);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          b200::bulk_g2s_stream(st + j * FP8_KB_BYTES,
-                                p.w + ((long long)(blk * 8 + j) * KB + kb) * FP8_KB_BYTES,
-                                FP8_KB_BYTES, &w_full[s], pol);
-        b200::bulk_g2s(st + TC_TILE_W, qt + (long long)kb * XT_BYTES, XT_BYTES, &w_full[s]);
+        issue_w(it);
+        issue_x(it);
         ++issued;
       }
       if (!ok) atomicExch(&g_lmhead_err, 1);
@@ -825,14 +904,12 @@ int num_sms() {
   return n;
 }
 
-constexpr int HDR = 128 + NC * MAXM * 12 + 16;   // barriers + per-warp stats + flag
-
-// Fill in the shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
-int plan(Params& p, bool is_w4, int nt8) {
+// Fill in the GEMV's shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
+int plan(Params& p, bool is_w4, int nt8, int nc) {
   const int KB = p.K / 128;
   const int rows_x = 8 * nt8;
   p.xs_stride = (is_w4 ? 2 * p.K : p.K) + 64;
-  p.xs_off = (HDR + 15) & ~15;
+  p.xs_off = (gemv_hdr(nc) + 15) & ~15;
   p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
   const int fixed = p.x_off + rows_x * p.xs_stride;
   const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
@@ -851,17 +928,36 @@ int plan(Params& p, bool is_w4, int nt8) {
   return -1;
 }
 
+// cudaLaunchKernelEx, optionally as the programmatic dependent of the previous kernel in the
+// stream (which must be one of ours that only produces this launch's activation).
+template <typename... Exp, typename... Act>
+int launch_ex(void (*kern)(Exp...), dim3 grid, dim3 block, int smem, cudaStream_t stream, bool pdl,
+              Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Act>(args)...);
+  return (int)(e != cudaSuccess ? e : cudaGetLastError());
+}
+
 template <int KIND, int NT8, bool STATS>
 int launch_one(Params p, cudaStream_t stream) {
   constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
-  const int smem = plan(p, IS_W4, NT8);
+  constexpr int NC = IS_W4 ? NC_W4 : NC_FP8;
+  const int smem = plan(p, IS_W4, NT8, NC);
   if (smem < 0) return -8;
-  auto kern = gemv_kernel<KIND, NT8, STATS>;
+  auto kern = gemv_kernel<KIND, NT8, STATS, NC>;
   cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int grid = min(p.N / 16, num_sms());
-  kern<<<grid, NTHREADS, smem, stream>>>(p);
-  return (int)cudaGetLastError();
+  return launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
 }
 
 template <int KIND, bool STATS>
@@ -870,11 +966,14 @@ int launch_m(const Params& p, cudaStream_t stream) {
 }
 
 // Workspace: [0,16) ticket counter | [16, 16+1024*64*12) per-CTA row statistics |
-// [QT_OFF, +QT_CAP) swizzled activation tiles | [XT_OFF, +XT_CAP) their scales.
+// [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
+// [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
-constexpr long long WORKSPACE_BYTES = XT_OFF + XT_CAP;
+constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
+constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
+constexpr long long WORKSPACE_BYTES = SR_OFF + SR_CAP;
 static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
 
 int plan_tc(Params& p, int tpad) {
@@ -890,24 +989,52 @@ int plan_tc(Params& p, int tpad) {
   return 1024 + p.ring_off + nstage * stage;
 }
 
+// 4-D view of the strip-packed weight for the tensor-map copy: (byte 128, row 16, kb, strip);
+// one (128, 16, 1, 8) box = the 128-row x 128-K tile, landing as [128 rows][128 B] already in
+// the 128-byte-swizzled order (the pack stores it that way, so the copy itself does not swizzle).
+int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return -12;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const int KB = K / 128;
+  cuuint64_t dims[4] = {128, 16, (cuuint64_t)KB, (cuuint64_t)(N / 16)};
+  cuuint64_t strides[3] = {128, 2048, (cuuint64_t)KB * 2048};
+  cuuint32_t box[4] = {128, 16, 1, 8};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(w), dims, strides, box,
+                            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -12;
+}
+
 template <int TPAD, bool STATS>
 int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t stream) {
   const int KB = p.K / 128;
   if ((long long)KB * TPAD * 128 > QT_CAP || (long long)TPAD * KB * 4 > XT_CAP) return -8;
+  if ((reinterpret_cast<uintptr_t>(p.w) & 127) != 0) return -10;
+  CUtensorMap wmap;
+  if (make_strip_map(&wmap, p.w, p.N, p.K) != 0) return -12;
   char* base = reinterpret_cast<char*>(p.counter);
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
-  act_tiles_kernel<<<dim3(KB, TPAD / 8), 128, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M, p.K, TPAD, qt,
-      xt, p.qx_out, p.xs_out);
+  int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,
+                     static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M,
+                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out);
+  if (rc != 0) return rc;
   const int smem = plan_tc(p, TPAD);
   if (smem < 0) return -8;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
   cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
+  p.pdl = 1;
   const int grid = min(p.N / 128, num_sms());
-  kern<<<grid, TC_THREADS, smem, stream>>>(p, qt, xt);
-  return (int)cudaGetLastError();
+  return launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
 }
 
 template <bool STATS>
@@ -916,15 +1043,16 @@ int launch_tc(const Params& p, const uint8_t* qx_in, const float* xs_in, cudaStr
                      : launch_tc_t<64, STATS>(p, qx_in, xs_in, stream);
 }
 
-// Runs M in token chunks, one weight pass each: FP8 with a workspace takes 64-token chunks and
-// sends every chunk above 16 tokens to the tcgen05 kernel; everything else goes through the
-// 16-token GEMV.
+// Runs M in token chunks, one weight pass each. With a workspace, FP8 takes 64-token chunks:
+// above 16 tokens the tcgen05 kernel, at most 16 the GEMV fed by act_rows_kernel (both as
+// programmatic dependents of their activation kernel). Without one, 16-token GEMV chunks.
 template <int KIND>
 int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
   const int M = p.M, KB = p.K / 128;
   const bool stats = (p.row_max || p.row_arg || p.row_lse);
-  const bool tc_ok = (KIND == FP8_QUANT || KIND == FP8_PREQ) && p.counter != nullptr &&
-                     (long long)KB * 64 * 128 <= QT_CAP;
+  const bool is_fp8 = (KIND == FP8_QUANT || KIND == FP8_PREQ);
+  const bool have_ws = p.counter != nullptr;
+  const bool tc_ok = is_fp8 && have_ws && (long long)KB * 64 * 128 <= QT_CAP;
   const int chunk = tc_ok ? 64 : MAXM;
   for (int m0 = 0; m0 < M; m0 += chunk) {
     Params q = p;
@@ -941,6 +1069,20 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
     if (tc_ok && q.M > MAXM) {
       const uint8_t* qx_in = (KIND == FP8_PREQ) ? static_cast<const uint8_t*>(q.x) : nullptr;
       rc = stats ? launch_tc<true>(q, qx_in, q.xs_in, stream) : launch_tc<false>(q, qx_in, q.xs_in, stream);
+    } else if (KIND == FP8_QUANT && have_ws && (long long)MAXM * p.K <= QR_CAP) {
+      // quantize the rows once (the programmatic primary), then the GEMV on e4m3 rows
+      char* base = reinterpret_cast<char*>(p.counter);
+      uint8_t* qr = q.qx_out ? q.qx_out : reinterpret_cast<uint8_t*>(base + QR_OFF);
+      float* sr = q.xs_out ? q.xs_out : reinterpret_cast<float*>(base + SR_OFF);
+      rc = launch_ex(act_rows_kernel, dim3(KB, (q.M + 7) / 8), dim3(128), 0, stream, false,
+                     static_cast<const __nv_bfloat16*>(q.x), q.M, q.K, qr, (float*)sr);
+      if (rc != 0) return rc;
+      q.x = qr;
+      q.xs_in = sr;
+      q.qx_out = nullptr;
+      q.xs_out = nullptr;
+      q.pdl = 1;
+      rc = stats ? launch_m<FP8_PREQ, true>(q, stream) : launch_m<FP8_PREQ, false>(q, stream);
     } else {
       rc = stats ? launch_m<KIND, true>(q, stream) : launch_m<KIND, false>(q, stream);
     }

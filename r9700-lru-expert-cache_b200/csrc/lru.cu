@@ -49,32 +49,36 @@ constexpr int MAXE_MANAGE = 65536;        // expert flags live in smem (E bytes)
 constexpr int SLOT_BITS = 20;             // r4d_lru.hip:29
 constexpr int SLOT_MASK = (1 << SLOT_BITS) - 1;
 constexpr long long KEY_MAX = 0x7fffffffffffffffLL;
+constexpr unsigned KEY32_MAX = 0xffffffffu;
+constexpr int AGE_BITS = 21;              // 32-bit keys: (2^21 - 1 - age) << 11 | slot
 constexpr int IDS_REG = 4;                // topk ids kept in registers: mk <= IDS_REG * NT
 
 // Shared-memory carve-up (bytes), all offsets 16-byte aligned.
 struct Smem {
-  int off_flags, off_tab, off_se, off_st, off_key, off_vic, off_missE;
-  int off_cnt_h, off_cum_h, off_cnt_c, off_cum_c, off_red, total;
+  int off_red, off_flags, off_tab, off_se, off_st, off_k64, off_k32, off_vic, off_missE;
+  int off_cnt_h, off_cum_h, off_cnt_c, off_cum_c, total;
 };
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
 
 __host__ __device__ inline Smem smem_layout(int E, int S, bool tab_smem, bool fused) {
   Smem L;
+  const int S4 = (S + 3) & ~3;
   int o = 0;
-  L.off_red = o;   o += align16(4 * 64 * (int)sizeof(int));
+  L.off_red = o;   o += align16(8 * NW * (int)sizeof(int));
   L.off_flags = o; o += align16(E);
   L.off_tab = o;   o += tab_smem ? align16(E * 4) : 0;
   L.off_se = o;    o += align16(S * 4);
   L.off_st = o;    o += align16(S * 8);
-  L.off_key = o;   o += align16(S * 8);
+  L.off_k64 = o;   o += align16(S4 * 8);
+  L.off_k32 = o;   o += align16(S4 * 4);
   L.off_vic = o;   o += align16(MAXINS * 4);
   L.off_missE = o; o += align16(MAXINS * 4);
   if (fused) {
     L.off_cnt_h = o; o += align16(S * 4);
-    L.off_cum_h = o; o += align16((S + 1) * 4);
+    L.off_cum_h = o; o += align16(S * 4);
     L.off_cnt_c = o; o += align16(E * 4);
-    L.off_cum_c = o; o += align16((E + 1) * 4);
+    L.off_cum_c = o; o += align16(E * 4);
   } else {
     L.off_cnt_h = L.off_cum_h = L.off_cnt_c = L.off_cum_c = 0;
   }
@@ -82,33 +86,30 @@ __host__ __device__ inline Smem smem_layout(int E, int S, bool tab_smem, bool fu
   return L;
 }
 
-// Block sum of one int per thread; `red` holds NW ints. One barrier; every thread returns
-// the total. `red` must not be reused before the next barrier.
-__device__ __forceinline__ int block_sum(int v, int* red) {
-  v = __reduce_add_sync(0xffffffffu, v);
-  if (b200::lane_id() == 0) red[threadIdx.x >> 5] = v;
+// Two-value block reduction in one barrier: per warp, a sum of `a` and an inclusive scan of
+// `b`; returns the block sum of a, the exclusive prefix of b, and the block total of b.
+// `ra`, `rb` hold NW ints each and must not be reused before the next barrier.
+__device__ __forceinline__ void block_sum_exscan(int a, int b, int* ra, int* rb, int* sum_a,
+                                                 int* pre_b, int* tot_b) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int wa = __reduce_add_sync(0xffffffffu, a);
+  const int inc = b200::warp_inclusive_scan(b);
+  if (l == 31) {
+    ra[w] = wa;
+    rb[w] = inc;
+  }
   __syncthreads();
-  int t = 0;
-#pragma unroll
-  for (int w = 0; w < NW; ++w) t += red[w];
-  return t;
-}
-
-// Exclusive block scan of one int per thread; one barrier; `red` holds NW ints.
-__device__ __forceinline__ int block_exscan(int v, int* red, int* total) {
-  const int inc = b200::warp_inclusive_scan(v);
-  const int w = threadIdx.x >> 5;
-  if (b200::lane_id() == 31) red[w] = inc;
-  __syncthreads();
-  int before = 0, t = 0;
+  int sa = 0, before = 0, tb = 0;
 #pragma unroll
   for (int i = 0; i < NW; ++i) {
-    const int x = red[i];
+    sa += ra[i];
+    const int x = rb[i];
     before += (i < w) ? x : 0;
-    t += x;
+    tb += x;
   }
-  *total = t;
-  return before + inc - v;
+  *sum_a = sa;
+  *pre_b = before + inc - b;
+  *tot_b = tb;
 }
 
 struct ManageArgs {
@@ -124,23 +125,25 @@ struct ManageArgs {
   int* n_miss;
 };
 
-// The manager, shared by both kernels. Every thread of the block calls it and every
-// thread returns (no early exit), so the fused kernel can carry on. On return the final
-// expert -> slot table is in s_tab when TAB_SMEM.
-template <bool TAB_SMEM>
+// The manager, shared by both kernels. Every thread of the block calls it and every thread
+// returns (no divergent exit). Six barriers. With FUSED the bucket counters are zeroed in the
+// first phase; on return the final expert -> slot table is in s_tab (TAB_SMEM).
+template <bool TAB_SMEM, bool FUSED>
 __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&ids)[IDS_REG]) {
   const int tid = threadIdx.x;
   const int E = a.E, S = a.S, mk = a.mk;
+  const int S4 = (S + 3) & ~3;
   unsigned char* flags = reinterpret_cast<unsigned char*>(sm + L.off_flags);
   int* s_tab = reinterpret_cast<int*>(sm + L.off_tab);
   int* s_se = reinterpret_cast<int*>(sm + L.off_se);
   long long* s_st = reinterpret_cast<long long*>(sm + L.off_st);
-  long long* s_key = reinterpret_cast<long long*>(sm + L.off_key);
+  long long* s_k64 = reinterpret_cast<long long*>(sm + L.off_k64);
+  unsigned* s_k32 = reinterpret_cast<unsigned*>(sm + L.off_k32);
   int* s_vic = reinterpret_cast<int*>(sm + L.off_vic);
   int* s_missE = reinterpret_cast<int*>(sm + L.off_missE);
   int* red = reinterpret_cast<int*>(sm + L.off_red);
 
-  // ---- issue every independent global load up front ----------------------------------
+  // ---- 1. every independent global load up front; clear the flags ------------------------
   const long long st = a.step[0] + 1;
 #pragma unroll
   for (int k = 0; k < IDS_REG; ++k) {
@@ -154,9 +157,15 @@ __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&
   if (TAB_SMEM)
     for (int i = tid; i < E; i += NT) s_tab[i] = a.table[i];
   for (int i = tid; i < E; i += NT) flags[i] = 0;
-  __syncthreads();
+  if (FUSED) {
+    int* cnt_h = reinterpret_cast<int*>(sm + L.off_cnt_h);
+    int* cnt_c = reinterpret_cast<int*>(sm + L.off_cnt_c);
+    for (int i = tid; i < S; i += NT) cnt_h[i] = 0;
+    for (int i = tid; i < E; i += NT) cnt_c[i] = 0;
+  }
+  __syncthreads();                                                          // B1
 
-  // ---- mark the routed experts ----------------------------------------------------------
+  // ---- 2. mark the routed experts -------------------------------------------------------
 #pragma unroll
   for (int k = 0; k < IDS_REG; ++k) {
     const int e = ids[k];
@@ -166,38 +175,32 @@ __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&
     const int e = a.topk[i];
     if (e >= 0 && e < E) flags[e] = 1;
   }
-  __syncthreads();
+  __syncthreads();                                                          // B2
 
-  // ---- distinct count, and the per-thread miss count over a contiguous expert chunk ----
+  // ---- 3. distinct count, hit stamps (shared copy only), misses in expert-id order ------
   const int C = (E + NT - 1) / NT;
-  const int lo = tid * C, hi = min(lo + C, E);
+  const int lo = min(tid * C, E), hi = min(lo + C, E);
   int cnt = 0, local = 0;
   for (int e = lo; e < hi; ++e) {
     const int f = flags[e];
-    a.routed[e] = (unsigned char)f;              // the reference leaves its scratch this way
-    cnt += f;
-    if (f) {
-      const int s = TAB_SMEM ? s_tab[e] : a.table[e];
-      local += (s < 0);
-    }
+    a.routed[e] = (unsigned char)f;
+    if (!f) continue;
+    ++cnt;
+    const int s = TAB_SMEM ? s_tab[e] : a.table[e];
+    if (s < 0)
+      ++local;
+    else if (s < S)
+      s_st[s] = st;                 // written back only if the call is not a read-through
   }
-  cnt = block_sum(cnt, red);
-  if (cnt > a.max_distinct) {                    // read-through: only step / n_miss change
+  int total_cnt, base, total;
+  block_sum_exscan(cnt, local, red, red + NW, &total_cnt, &base, &total);   // B3
+  if (total_cnt > a.max_distinct) {                 // read-through: only step / n_miss change
     if (tid == 0) {
       a.step[0] = st;
       a.n_miss[0] = 0;
     }
     return;
   }
-
-  // ---- hits refresh their stamp; misses enumerated in expert-id order ------------------
-  for (int e = lo; e < hi; ++e) {
-    if (!flags[e]) continue;
-    const int s = TAB_SMEM ? s_tab[e] : a.table[e];
-    if (s >= 0 && s < S) s_st[s] = st;
-  }
-  int total = 0;
-  const int base = block_exscan(local, red + NW, &total);
   const int nins = min(total, a.max_inserts);
   if (nins > 0) {
     int j = base;
@@ -219,42 +222,77 @@ __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&
     return;
   }
 
-  // ---- victim keys: (stamp << 20) | slot, or KEY_MAX when the slot's expert is routed ----
-  int nev = 0;
-  for (int i = tid; i < S; i += NT) {
-    const int se = s_se[i];
-    const bool busy = (se >= 0 && se < E && flags[se]);
-    s_key[i] = busy ? KEY_MAX : ((s_st[i] << SLOT_BITS) | (long long)i);
-    nev += busy ? 0 : 1;
+  // ---- 4. victim keys: (stamp << 20) | slot, and the order-equivalent 32-bit form ---------
+  // ((2^21 - 1 - (step - stamp)) << 11) | slot, valid when every evictable stamp is within
+  // 2^21 steps of the current one (checked; otherwise the 64-bit keys are ranked).
+  int nev = 0, nofit = 0;
+  for (int i = tid; i < S4; i += NT) {
+    long long k64 = KEY_MAX;
+    unsigned k32 = KEY32_MAX;
+    if (i < S) {
+      const int se = s_se[i];
+      const bool busy = (se >= 0 && se < E && flags[se]);
+      if (!busy) {
+        const long long stamp = s_st[i];
+        const long long age = st - stamp;
+        k64 = (stamp << SLOT_BITS) | (long long)i;
+        if (age >= 0 && age < (1LL << AGE_BITS))
+          k32 = ((unsigned)((1LL << AGE_BITS) - 1 - age) << 11) | (unsigned)i;
+        else
+          ++nofit;
+        ++nev;
+      }
+    }
+    s_k64[i] = k64;
+    s_k32[i] = k32;
   }
-  nev = block_sum(nev, red + 2 * NW);           // the barrier also publishes s_key / s_missE
-  const int nact = min(nins, nev);
+  int nev_total, dummy, nofit_total;
+  block_sum_exscan(nev, nofit, red + 2 * NW, red + 3 * NW, &nev_total, &dummy, &nofit_total);  // B4
+  const int nact = min(nins, nev_total);
 
-  // ---- rank every evictable key against the whole array: rank r < nins -> victim r ------
-  {
-    const int i0 = tid, i1 = tid + NT;
-    const long long k0 = (i0 < S) ? s_key[i0] : KEY_MAX;
-    const long long k1 = (i1 < S) ? s_key[i1] : KEY_MAX;
-    int r0 = 0, r1 = 0;
-    const longlong2* kv = reinterpret_cast<const longlong2*>(s_key);
-    const int S2 = S >> 1;
+  // ---- 5. rank each evictable key against all keys: rank r < nins -> victim r -------------
+  if (nofit_total == 0) {
+    const unsigned k0 = (tid < S) ? s_k32[tid] : KEY32_MAX;
+    const unsigned k1 = (tid + NT < S) ? s_k32[tid + NT] : KEY32_MAX;
+    if (k0 != KEY32_MAX || k1 != KEY32_MAX) {
+      const uint4* kv = reinterpret_cast<const uint4*>(s_k32);
+      int r0 = 0, r1 = 0;
+      if (S <= NT) {
+#pragma unroll 8
+        for (int j = 0; j < (S4 >> 2); ++j) {
+          const uint4 q = kv[j];
+          r0 += (q.x < k0) + (q.y < k0) + (q.z < k0) + (q.w < k0);
+        }
+      } else {
 #pragma unroll 4
-    for (int j = 0; j < S2; ++j) {
-      const longlong2 p = kv[j];
-      r0 += (p.x < k0) + (p.y < k0);
-      r1 += (p.x < k1) + (p.y < k1);
+        for (int j = 0; j < (S4 >> 2); ++j) {
+          const uint4 q = kv[j];
+          r0 += (q.x < k0) + (q.y < k0) + (q.z < k0) + (q.w < k0);
+          r1 += (q.x < k1) + (q.y < k1) + (q.z < k1) + (q.w < k1);
+        }
+      }
+      if (k0 != KEY32_MAX && r0 < nins) s_vic[r0] = tid;
+      if (k1 != KEY32_MAX && r1 < nins) s_vic[r1] = tid + NT;
     }
-    if (S & 1) {
-      const long long p = s_key[S - 1];
-      r0 += (p < k0);
-      r1 += (p < k1);
+  } else {
+    const long long k0 = (tid < S) ? s_k64[tid] : KEY_MAX;
+    const long long k1 = (tid + NT < S) ? s_k64[tid + NT] : KEY_MAX;
+    if (k0 != KEY_MAX || k1 != KEY_MAX) {
+      const longlong2* kv = reinterpret_cast<const longlong2*>(s_k64);
+      int r0 = 0, r1 = 0;
+#pragma unroll 4
+      for (int j = 0; j < (S4 >> 1); ++j) {
+        const longlong2 q = kv[j];
+        r0 += (q.x < k0) + (q.y < k0);
+        r1 += (q.x < k1) + (q.y < k1);
+      }
+      if (k0 != KEY_MAX && r0 < nins) s_vic[r0] = tid;
+      if (k1 != KEY_MAX && r1 < nins) s_vic[r1] = tid + NT;
     }
-    if (k0 != KEY_MAX && r0 < nins) s_vic[r0] = i0;
-    if (k1 != KEY_MAX && r1 < nins) s_vic[r1] = i1;
   }
-  __syncthreads();
+  __syncthreads();                                                          // B5
 
-  // ---- install the victims in parallel (r4d_lru.hip:102-117) -----------------------------
+  // ---- 6. install the victims in parallel (r4d_lru.hip:102-117) -----------------------------
   // victim slots are distinct, missing experts are distinct, and an evicted expert is not
   // routed while every inserted one is, so no two threads touch the same entry.
   for (int r = tid; r < nact; r += NT) {
@@ -273,7 +311,7 @@ __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&
     a.map_cold[e] = -1;
     a.miss[2 * r + 1] = sl;
   }
-  __syncthreads();
+  __syncthreads();                                                          // B6
   for (int i = tid; i < S; i += NT) {
     a.slot_expert[i] = s_se[i];
     a.slot_stamp[i] = s_st[i];
@@ -289,7 +327,7 @@ __global__ void __launch_bounds__(NT) lru_manage_kernel(ManageArgs a) {
   extern __shared__ __align__(16) char sm[];
   const Smem L = smem_layout(a.E, a.S, TAB_SMEM, false);
   int ids[IDS_REG];
-  manage_core<TAB_SMEM>(a, sm, L, ids);
+  manage_core<TAB_SMEM, false>(a, sm, L, ids);
 }
 
 struct FusedArgs {
@@ -303,15 +341,21 @@ struct FusedArgs {
   int* npad_cold;
 };
 
-// One side's block-padded bucket bookkeeping: pad fills of sorted_ids and expert_ids for the
-// buckets [lo, hi) this thread owns (the non-padding slots are written by placement).
-__device__ __forceinline__ void fill_side(int lo, int hi, const int* cnt, const int* cum, int bs,
-                                          int mk, int Lcap, int NBcap, int* sorted, int* eids) {
+// One side's padding: sorted_ids sentinels after each bucket's tokens and the bucket id of
+// each of its blocks, for the buckets [lo, hi) this thread owns; then the counts become the
+// placement cursors (same owner, so no other thread reads them meanwhile).
+__device__ __forceinline__ int fill_side(int lo, int hi, int* cnt, int* cum, int run, int bs,
+                                         int mk, int Lcap, int NBcap, int* sorted, int* eids) {
   for (int b = lo; b < hi; ++b) {
-    const int c0 = cum[b], c1 = cum[b + 1];
-    for (int p = c0 + cnt[b]; p < c1 && p < Lcap; ++p) sorted[p] = mk;
-    for (int blk = c0 / bs; blk < c1 / bs && blk < NBcap; ++blk) eids[blk] = b;
+    const int c = cnt[b];
+    const int pad = (c + bs - 1) / bs * bs;
+    cum[b] = run;
+    for (int p = run + c; p < run + pad && p < Lcap; ++p) sorted[p] = mk;
+    for (int blk = run / bs; blk < (run + pad) / bs && blk < NBcap; ++blk) eids[blk] = b;
+    cnt[b] = run;
+    run += pad;
   }
+  return run;
 }
 
 __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
@@ -322,9 +366,11 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
   const int tid = threadIdx.x;
   int ids[IDS_REG];
 
-  // ---- phase 0: the manager (single exit: every output below is always written) --------
-  manage_core<true>(a, sm, L, ids);
-  __syncthreads();
+  // ---- the manager (single exit: every output below is always written) ------------------
+  // Its last barrier orders the table installs before the reads below; on its early exits
+  // the shared table is unchanged since its second barrier, and the counters were zeroed in
+  // its first phase.
+  manage_core<true, true>(a, sm, L, ids);
 
   const int* s_tab = reinterpret_cast<const int*>(sm + L.off_tab);
   int* cnt_h = reinterpret_cast<int*>(sm + L.off_cnt_h);
@@ -333,10 +379,6 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
   int* cum_c = reinterpret_cast<int*>(sm + L.off_cum_c);
   int* red = reinterpret_cast<int*>(sm + L.off_red);
 
-  for (int i = tid; i < S; i += NT) cnt_h[i] = 0;
-  for (int i = tid; i < E; i += NT) cnt_c[i] = 0;
-  __syncthreads();
-
   // bucket key of token i: slot (hot) or MAXS + expert (cold); -1 = ignored
   auto bucket_of = [&](int e) -> int {
     if (e < 0 || e >= E) return -1;
@@ -344,7 +386,7 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
     return ((unsigned)s < (unsigned)S) ? s : (MAXS + e);
   };
 
-  // ---- phase 2: counts (smem atomics: the counts do not depend on the order) -------------
+  // ---- counts (shared atomics: the counts do not depend on the order) --------------------
 #pragma unroll
   for (int k = 0; k < IDS_REG; ++k) {
     const int b = bucket_of(ids[k]);
@@ -356,49 +398,50 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
   }
   __syncthreads();
 
-  // ---- phase 3: block-padded exclusive scans of both sides in one block scan ------------
+  // ---- block-padded exclusive scans of both sides in one barrier --------------------------
   const int Ch = (S + NT - 1) / NT, Cc = (E + NT - 1) / NT;
   const int lh = min(tid * Ch, S), hh = min(lh + Ch, S);
   const int lc = min(tid * Cc, E), hc = min(lc + Cc, E);
   int sh = 0, sc = 0;
   for (int b = lh; b < hh; ++b) sh += (cnt_h[b] + bs - 1) / bs * bs;
   for (int b = lc; b < hc; ++b) sc += (cnt_c[b] + bs - 1) / bs * bs;
-  int tot_h = 0, tot_c = 0;
-  const int eh = block_exscan(sh, red, &tot_h);
-  const int ec = block_exscan(sc, red + NW, &tot_c);
+  int eh, ec, tot_h, tot_c;
   {
-    int run = eh;
-    for (int b = lh; b < hh; ++b) {
-      cum_h[b] = run;
-      run += (cnt_h[b] + bs - 1) / bs * bs;
+    const int w = tid >> 5, l = tid & 31;
+    const int ih = b200::warp_inclusive_scan(sh), ic = b200::warp_inclusive_scan(sc);
+    if (l == 31) {
+      red[4 * NW + w] = ih;
+      red[5 * NW + w] = ic;
     }
-    run = ec;
-    for (int b = lc; b < hc; ++b) {
-      cum_c[b] = run;
-      run += (cnt_c[b] + bs - 1) / bs * bs;
+    __syncthreads();
+    int bh = 0, bc = 0;
+    tot_h = tot_c = 0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const int xh = red[4 * NW + i], xc = red[5 * NW + i];
+      bh += (i < w) ? xh : 0;
+      bc += (i < w) ? xc : 0;
+      tot_h += xh;
+      tot_c += xc;
     }
-    if (tid == 0) {
-      cum_h[S] = tot_h;
-      cum_c[E] = tot_c;
-      f.npad_hot[0] = tot_h;
-      f.npad_cold[0] = tot_c;
-    }
+    eh = bh + ih - sh;
+    ec = bc + ic - sc;
   }
-  __syncthreads();
+  if (tid == 0) {
+    f.npad_hot[0] = tot_h;
+    f.npad_cold[0] = tot_c;
+  }
 
-  // ---- phase 4: expert_ids and padding sentinels; tail past npad --------------------------
-  fill_side(lh, hh, cnt_h, cum_h, bs, mk, f.L, f.NB, f.sorted_hot, f.eids_hot);
-  fill_side(lc, hc, cnt_c, cum_c, bs, mk, f.L, f.NB, f.sorted_cold, f.eids_cold);
+  // ---- expert_ids, padding sentinels, tails; counts become cursors -------------------------
+  fill_side(lh, hh, cnt_h, cum_h, eh, bs, mk, f.L, f.NB, f.sorted_hot, f.eids_hot);
+  fill_side(lc, hc, cnt_c, cum_c, ec, bs, mk, f.L, f.NB, f.sorted_cold, f.eids_cold);
   for (int p = tot_h + tid; p < f.L; p += NT) f.sorted_hot[p] = mk;
   for (int p = tot_c + tid; p < f.L; p += NT) f.sorted_cold[p] = mk;
   for (int blk = tot_h / bs + tid; blk < f.NB; blk += NT) f.eids_hot[blk] = -1;
   for (int blk = tot_c / bs + tid; blk < f.NB; blk += NT) f.eids_cold[blk] = -1;
-
-  // ---- phase 5: stable placement; cnt_* become the running cursors -----------------------
-  // (same bucket ownership as fill_side, so each thread overwrites only counts it has read)
-  for (int b = lh; b < hh; ++b) cnt_h[b] = cum_h[b];
-  for (int b = lc; b < hc; ++b) cnt_c[b] = cum_c[b];
   __syncthreads();
+
+  // ---- stable placement: warp match_any ranks, warps advance the cursors in order --------
   const int warp = tid >> 5;
   const unsigned lt = b200::lanemask_lt();
   for (int base = 0, k = 0; base < mk; base += NT, ++k) {
@@ -419,10 +462,9 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const int rank = __popc(peers & lt);
         int* cur = nullptr;
-        int pos = 0;
         if (key >= 0) {
           cur = key < MAXS ? &cnt_h[key] : &cnt_c[key - MAXS];
-          pos = *cur + rank;
+          const int pos = *cur + rank;
           if (pos < f.L) (key < MAXS ? f.sorted_hot : f.sorted_cold)[pos] = i;
         }
         __syncwarp();
@@ -474,7 +516,6 @@ __global__ void __launch_bounds__(GNT) lru_gather_kernel(GatherArgs g) {
   }
 }
 
-bool g_attr_done[2] = {false, false};
 
 }  // namespace
 
