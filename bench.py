@@ -228,7 +228,12 @@ def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
             times.append(a.elapsed_time(b) * 1e3 / LAYERS)
             ins += sum(int(l.n_miss.item()) for l in layers)
     del g
-    return {"us_per_layer": statistics.median(times), "layers": LAYERS, "experts_per_gpu": e_loc,
+    # floor: the same number of empty launches in one graph (hcq_stream_probe over 0 bytes)
+    buf = torch.zeros(16, dtype=torch.uint8, device=dev)
+    nul = lambda: P._lib.lmhead().hcq_stream_probe(P._lib.ptr(buf), 0, 1, P._lib.ptr(buf), P._lib.stream_ptr())
+    floor = time_graph(nul, LAYERS, dev)
+    return {"us_per_layer": statistics.median(times), "empty_launch_floor_us": floor,
+            "layers": LAYERS, "experts_per_gpu": e_loc,
             "slots_per_gpu": s_loc, "mk": mk, "inserts_per_layer_step": ins / (len(times) * LAYERS),
             "method": "52 fused launches in one CUDA graph, median over replays"}
 
@@ -407,11 +412,13 @@ def main():
             for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         start.record()
         for i in range(args.steps):
             step(i, kevs[i])
         end.record()
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)

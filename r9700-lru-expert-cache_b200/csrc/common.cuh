@@ -93,18 +93,27 @@ B200_DEVINL bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase. Returns false if `deadline_ns` (globaltimer) passed
-// first; the caller then records an error and leaves instead of spinning forever.
+B200_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. try_wait suspends the thread in hardware until the phase
+// completes or a short system time limit passes, so a waiting warp costs no issue slots and
+// wakes as soon as the phase flips. Returns false once `deadline_ns` (globaltimer) has passed;
+// the caller then records an error and leaves instead of waiting forever.
 B200_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
-  if (mbar_test_wait(bar, parity)) return true;
-  uint32_t spins = 0;
-  while (true) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if (++spins > 64) {
-      __nanosleep(64);
-      if ((spins & 255u) == 0 && globaltimer_ns() > deadline_ns) return false;
-    }
+  uint32_t n = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++n & 15u) == 0 && globaltimer_ns() > deadline_ns) return false;
   }
+  return true;
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (transaction bytes).

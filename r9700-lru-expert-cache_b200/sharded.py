@@ -57,8 +57,13 @@ def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, gr
     rank (24 B/row) in one collective; every rank returns the global triple."""
     world = dist.get_world_size(group)
     local = torch.stack([mx.double(), arg.double(), lse.double()], dim=1).contiguous()
-    gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(gathered, local, group=group)
+    if local.is_cuda:
+        gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(gathered, local, group=group)
+    else:                                   # gloo (host-side tests of the combine)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local, group=group)
+        gathered = torch.stack(parts)
     return _combine(gathered[:, :, 0], gathered[:, :, 1].to(torch.int64), gathered[:, :, 2])
 
 
