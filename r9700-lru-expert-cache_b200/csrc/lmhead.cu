@@ -47,7 +47,7 @@ constexpr int NC_FP8 = 4;                // consumer warps of the FP8 GEMV
 constexpr int NC_W4 = 8;                 // consumer warps of the W4 GEMV (more ALU per byte)
 constexpr int MAXM = 16;                 // tokens per GEMV launch
 constexpr int SMEM_CAP = 227 * 1024;
-constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES = 16;
 constexpr int FP8_KB_BYTES = 16 * 128;   // one strip x one 128-K block
 constexpr int W4_KB_BYTES = 16 * 64;
 constexpr int W4_SZ_BYTES = 16 * 4;
@@ -333,9 +333,10 @@ __device__ void stats_finalize(const Params& p, const b200::RowStat* red, int st
 
 // ---- the kernel ------------------------------------------------------------------------------
 
-// Shared-memory header of the GEMV: full/empty barriers [0, 128), the activation barrier at
-// 128, per-warp row statistics from 256, the "last CTA" flag after them.
-constexpr int GEMV_HDR_RED = 256;
+// Shared-memory header of the GEMV: full/empty barriers [0, 256), the activation barrier at
+// 256, per-warp row statistics from 384, the "last CTA" flag after them.
+constexpr int GEMV_XBAR = 256;
+constexpr int GEMV_HDR_RED = 384;
 __host__ __device__ constexpr int gemv_hdr(int nc) { return GEMV_HDR_RED + nc * MAXM * 12 + 16; }
 
 template <int KIND, int NT8, bool STATS, int NC>
@@ -353,7 +354,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 
   uint64_t* full = reinterpret_cast<uint64_t*>(sm);
   uint64_t* empty = full + MAX_STAGES;
-  uint64_t* x_bar = reinterpret_cast<uint64_t*>(sm + 128);
+  uint64_t* x_bar = reinterpret_cast<uint64_t*>(sm + GEMV_XBAR);
   b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + GEMV_HDR_RED);   // [NC][MAXM]
   int* s_flag = reinterpret_cast<int*>(sm + GEMV_HDR_RED + NC * MAXM * sizeof(b200::RowStat));
   char* ring = sm + p.ring_off;
@@ -836,30 +837,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       if (!ok) break;
-      const int n = blk * 128 + 32 * qd + lane;
-      if (p.y != nullptr) {
+      // Block epilogue through a per-warp [32][33] shared tile: lanes hold rows on the way in
+      // and tokens on the way out, so each lane stores 32 consecutive logits of one token
+      // (64 contiguous bytes) and updates that token's (max, argmax, sum exp) over its 32
+      // rows in increasing row order -- no cross-lane reduction per token.
+      float* tr = reinterpret_cast<float*>(sm + p.x_off) + ew * (32 * 33);
+      const int n0 = blk * 128 + 32 * qd;
 #pragma unroll
-        for (int j = 0; j < TPAD; ++j)
-          if (j < p.M) p.y[(long long)j * p.ldy + n] = __float2bfloat16_rn(acc[j]);
-      }
-      if (STATS) {
-        const int base = (int)(blk * 128 + 32 * qd + p.vocab_offset);
+      for (int c = 0; c < TPAD / 32; ++c) {
 #pragma unroll
-        for (int j = 0; j < TPAD; ++j) {
-          if (j < p.M) {
-            const float v = acc[j];
-            const float wm = b200::warp_max(v);
-            const unsigned bal = __ballot_sync(0xffffffffu, v == wm);
-            const float es = b200::warp_sum(expf(v - wm));
-            if (lane == (j & 31)) {
-              b200::RowStat o;
-              o.m = wm;
-              o.idx = base + __ffs(bal) - 1;
-              o.s = es;
-              st[j >> 5] = b200::rowstat_merge(st[j >> 5], o);
+        for (int j = 0; j < 32; ++j) tr[j * 33 + lane] = acc[32 * c + j];
+        __syncwarp();
+        const int t = 32 * c + lane;
+        if (t < p.M) {
+          float v[32];
+#pragma unroll
+          for (int r = 0; r < 32; ++r) v[r] = tr[lane * 33 + r];
+          if (p.y != nullptr) {
+            uint4* dst = reinterpret_cast<uint4*>(p.y + (long long)t * p.ldy + n0);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              __nv_bfloat162 h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[8 * q4 + 2 * i], v[8 * q4 + 2 * i + 1]);
+              dst[q4] = *reinterpret_cast<const uint4*>(h);
             }
           }
+          if (STATS) {
+            const int base = (int)(n0 + p.vocab_offset);
+#pragma unroll
+            for (int r = 0; r < 32; ++r) b200::rowstat_push(st[c], v[r], base + r);
+          }
         }
+        __syncwarp();
       }
     }
     if (!ok) atomicExch(&g_lmhead_err, 1);
@@ -913,11 +923,15 @@ int plan(Params& p, bool is_w4, int nt8, int nc) {
   p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
   const int fixed = p.x_off + rows_x * p.xs_stride;
   const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
-  for (int kps = min(KB, 24); kps >= 1; --kps) {
+  // Every consumer warp holds one stage while it works on it, so the ring needs more stages
+  // than consumers: W4 (8 consumers) takes half-strip stages, FP8 (4) whole strips.
+  const int want = is_w4 ? nc + 2 : 4;
+  const int kmax = is_w4 ? (KB + 1) / 2 : KB;
+  for (int kps = min(kmax, 24); kps >= 1; --kps) {
     const int sb = (kps * per_kb + 127) & ~127;
     const int ring_off = (fixed + 127) & ~127;
     const int nstage = min(MAX_STAGES, (SMEM_CAP - ring_off) / sb);
-    if (nstage >= 3 || (kps == 1 && nstage >= 2)) {
+    if (nstage >= want || (kps == 1 && nstage >= 2)) {
       p.kps = kps;
       p.stage_bytes = sb;
       p.nstage = nstage;
@@ -979,7 +993,8 @@ static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
 int plan_tc(Params& p, int tpad) {
   const int KB = p.K / 128;
   p.xs_off = TC_HDR + TC_RED;
-  p.ring_off = (p.xs_off + tpad * KB * 4 + 1023) & ~1023;
+  p.x_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;          // 4 warps x [32][33] fp32 tiles
+  p.ring_off = (p.x_off + 4 * 32 * 33 * 4 + 1023) & ~1023;
   const int stage = TC_TILE_W + tpad * 128;
   const int avail = SMEM_CAP - 1024 - p.ring_off;
   const int nstage = min(TC_MAX_STAGES, avail / stage);
@@ -1018,6 +1033,7 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   const int KB = p.K / 128;
   if ((long long)KB * TPAD * 128 > QT_CAP || (long long)TPAD * KB * 4 > XT_CAP) return -8;
   if ((reinterpret_cast<uintptr_t>(p.w) & 127) != 0) return -10;
+  if (p.y != nullptr && ((p.ldy % 8) != 0 || (reinterpret_cast<uintptr_t>(p.y) & 15) != 0)) return -10;
   CUtensorMap wmap;
   if (make_strip_map(&wmap, p.w, p.N, p.K) != 0) return -12;
   char* base = reinterpret_cast<char*>(p.counter);
