@@ -199,9 +199,10 @@ B200_DEVINL void rowstat_init(RowStat& r) {
   r.s = 0.f;
 }
 
-// Values must arrive in increasing index order per state for the first-index tie rule.
+// Push one logit. A tie with the running max keeps the smaller index, so the result does not
+// depend on the order in which rows arrive.
 B200_DEVINL void rowstat_push(RowStat& r, float v, int idx) {
-  if (v > r.m) {
+  if (v > r.m || (v == r.m && idx < r.idx)) {
     r.s = r.s * expf(r.m - v) + 1.f;
     r.m = v;
     r.idx = idx;

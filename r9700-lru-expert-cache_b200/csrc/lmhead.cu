@@ -923,11 +923,9 @@ int plan(Params& p, bool is_w4, int nt8, int nc) {
   p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
   const int fixed = p.x_off + rows_x * p.xs_stride;
   const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
-  // Every consumer warp holds one stage while it works on it, so the ring needs more stages
-  // than consumers: W4 (8 consumers) takes half-strip stages, FP8 (4) whole strips.
-  const int want = is_w4 ? nc + 2 : 4;
-  const int kmax = is_w4 ? (KB + 1) / 2 : KB;
-  for (int kps = min(kmax, 24); kps >= 1; --kps) {
+  // Whole-strip stages (one bulk copy of weights per stage), as deep a ring as fits.
+  const int want = 4;
+  for (int kps = min(KB, 24); kps >= 1; --kps) {
     const int sb = (kps * per_kb + 127) & ~127;
     const int ring_off = (fixed + 127) & ~127;
     const int nstage = min(MAX_STAGES, (SMEM_CAP - ring_off) / sb);
