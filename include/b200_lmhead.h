@@ -56,6 +56,16 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
                     float* row_lse, void* qx_out, float* xs_out, void* workspace,
                     long long workspace_bytes, cudaStream_t stream);
 
+/* b200_fp8_lmhead without the workspace argument: the scratch is a device array inside the
+ * library (about 2.4 MB per device), for callers that cannot allocate device memory. No
+ * counterpart in the reference. Extra codes: -9 K > 16384, -13 device index >= 64. The first
+ * call per device looks the array up; one array serves all streams of a device, so calls must
+ * not overlap on the GPU. */
+int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
+                                   int N, long long vocab_offset, void* y, long long ldy,
+                                   float* row_max, int* row_arg, float* row_lse, void* qx_out,
+                                   float* xs_out, cudaStream_t stream);
+
 /* The closed fp8hip GEMM's ABI (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K]
  * and fp32 xs [M, K/128], packed w / ws, bf16 y [M, N]. */
 int fp8hip_gemm_w8a8_launch(void* qx, void* w, void* xs, void* ws, void* y, int M, int N, int K,

@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <utility>
 
 #include "common.cuh"
@@ -1252,5 +1253,72 @@ void r4d_gemm_w4a16_nt_m64(long a, long wq, long wsz, long c, int M, int K, int 
 int r4d_gemm_w4a16_nt_m64_last_error(void) { return g_w4_last_rc; }
 int r4d_gemm_w4a16_nt_m64_max_m(void) { return 64; }
 int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
+
+}  // extern "C"
+
+// ---- FP8 lm_head with built-in scratch (allocates nothing) ----------------------------------
+//
+// b200_fp8_lmhead needs a caller-owned workspace. Some callers cannot hand one over: a plain C
+// or ctypes binding that has no device allocator of its own, or code running where an
+// allocation is not allowed (a caching allocator's hook, a memory-capped pool). For those the
+// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 2.4 MB per
+// device, reserved when the library's device code is loaded).
+
+namespace {
+
+constexpr long long STATIC_SCRATCH_BYTES = WORKSPACE_BYTES;
+constexpr int STATIC_SCRATCH_MAX_K = 16384;     // tcgen05 tiles and GEMV rows both fit
+constexpr int STATIC_SCRATCH_MAX_DEVICES = 64;
+static_assert((long long)(STATIC_SCRATCH_MAX_K / 128) * 64 * 128 <= QT_CAP, "tile region");
+static_assert((long long)MAXM * STATIC_SCRATCH_MAX_K <= QR_CAP, "row region");
+
+static __device__ __align__(256) unsigned char g_static_scratch[STATIC_SCRATCH_BYTES];
+void* g_static_scratch_ptr[STATIC_SCRATCH_MAX_DEVICES] = {};
+std::mutex g_static_scratch_mu;
+
+// Device address of this device's copy of the array, looked up on the first call made with
+// that device current. Returns 0, -13 device index beyond the table, or the CUDA error.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= STATIC_SCRATCH_MAX_DEVICES) return -13;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_static_scratch_ptr[dev] = ptr;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+// b200_fp8_lmhead with the library's own scratch instead of a workspace argument; same
+// operands, outputs and return codes, plus -9 K > STATIC_SCRATCH_MAX_K and -13 device index
+// >= 64. The first call on each device looks the scratch up (make it before capturing a
+// stream). Every call first clears the scratch's ticket counter on `stream`. One array serves
+// every stream of a device, so calls that overlap on the GPU race on it: run them in order.
+int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
+                                   int N, long long vocab_offset, void* y, long long ldy,
+                                   float* row_max, int* row_arg, float* row_lse, void* qx_out,
+                                   float* xs_out, cudaStream_t stream) {
+  if (M < 0) return -1;
+  if (N <= 0 || N % 128) return -2;
+  if (K <= 0 || K % 128) return -3;
+  if (K > STATIC_SCRATCH_MAX_K) return -9;
+  if (M == 0) return 0;
+  void* scratch = nullptr;
+  const int rc = static_scratch(&scratch);
+  if (rc != 0) return rc;
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, 16, stream);
+  if (e != cudaSuccess) return (int)e;
+  return b200_fp8_lmhead(x, M, K, wq, ws, N, vocab_offset, y, ldy, row_max, row_arg, row_lse,
+                         qx_out, xs_out, scratch, STATIC_SCRATCH_BYTES, stream);
+}
 
 }  // extern "C"
