@@ -227,6 +227,37 @@ B200_DEVINL RowStat rowstat_merge(const RowStat& a, const RowStat& b) {
   return o;
 }
 
+// Push 32 consecutive logits (indices idx0 .. idx0 + 31) at once: their max and first argmax
+// by trees over independent values and the sum of exp by 32 independent exponentials, then one
+// merge -- a short dependency chain instead of 32 dependent exponentials.
+B200_DEVINL void rowstat_push32(RowStat& r, const float (&v)[32], int idx0) {
+  float t[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) t[i] = fmaxf(v[i], v[i + 16]);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
+  }
+  const float m = t[0];
+  int ir = 31;
+#pragma unroll
+  for (int i = 31; i >= 0; --i) ir = (v[i] == m) ? i : ir;
+  float e[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) e[i] = expf(v[i] - m) + expf(v[i + 16] - m);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) e[i] += e[i + w];
+  }
+  RowStat b;
+  b.m = m;
+  b.idx = idx0 + ir;
+  b.s = e[0];
+  r = rowstat_merge(r, b);
+}
+
 B200_DEVINL RowStat rowstat_shfl_xor(const RowStat& r, int mask) {
   RowStat o;
   o.m = __shfl_xor_sync(0xffffffffu, r.m, mask);

@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 #include <utility>
 
@@ -80,6 +81,8 @@ struct Params {
   int xs_stride;     // bytes per activation row in shared memory
   int x_off, xs_off, ring_off;
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
+  int kw;            // tcgen05 path: 128-K blocks per stage
+  float* px;         // tcgen05 path: partial accumulators of blocks split along K
 };
 
 template <int NC>
@@ -285,23 +288,34 @@ __device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32
 }
 
 // ---- row statistics: CTA partial per token, then the last CTA to finish merges them ---------
-// red[w * stride + m] holds warp w's state for token m (nred warps). Call with every thread
-// of the CTA after a barrier that published `red`. The workspace partials are token-major
-// ([m][cta]) so the final merge reads them coalesced; the last CTA resets the ticket.
-__device__ void stats_finalize(const Params& p, const b200::RowStat* red, int stride, int nred,
-                               int* s_flag) {
-  const int G = gridDim.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+// red[w * stride + m] holds warp w's state for token m (nred warps). The workspace partials
+// are token-major ([m][slot], G slots) so the final merge reads them coalesced.
+
+// Write this CTA's merged state per token into partial slot `slot`. Every thread calls it
+// after a barrier that published `red`.
+__device__ __forceinline__ void stats_write_partial(const Params& p, const b200::RowStat* red, int stride,
+                                                    int nred, int slot, int G) {
   if (threadIdx.x < p.M) {
     const int m = threadIdx.x;
     b200::RowStat r = red[m];
     for (int w = 1; w < nred; ++w) r = b200::rowstat_merge(r, red[w * stride + m]);
-    float* dst = p.partial + ((long long)m * G + blockIdx.x) * 3;
+    float* dst = p.partial + ((long long)m * G + slot) * 3;
     dst[0] = r.m;
     dst[1] = __int_as_float(r.idx);
     dst[2] = r.s;
-    __threadfence();
   }
+}
+
+// Merge all G partial slots per token into row_max / row_arg / row_lse (one CTA).
+__device__ void stats_merge_all(const Params& p, int G);
+
+// Partial into slot blockIdx.x of gridDim.x, then a ticket; the last CTA of the grid merges
+// and resets the ticket.
+__device__ void stats_finalize(const Params& p, const b200::RowStat* red, int stride, int nred,
+                               int* s_flag) {
+  const int G = gridDim.x;
+  stats_write_partial(p, red, stride, nred, blockIdx.x, G);
+  if (threadIdx.x < p.M) __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned ticket = atomicAdd(p.counter, 1u);
@@ -310,26 +324,63 @@ __device__ void stats_finalize(const Params& p, const b200::RowStat* red, int st
   __syncthreads();
   if (*s_flag == 0) return;
   __threadfence();
-  for (int m = warp; m < p.M; m += nwarps) {
-    b200::RowStat r;
-    b200::rowstat_init(r);
-    for (int c = lane; c < G; c += 32) {
-      const float* src = p.partial + ((long long)m * G + c) * 3;
-      b200::RowStat o;
-      o.m = __ldcg(src);
-      o.idx = __float_as_int(__ldcg(src + 1));
-      o.s = __ldcg(src + 2);
-      r = b200::rowstat_merge(r, o);
+  stats_merge_all(p, G);
+  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
+}
+
+__device__ void stats_merge_all(const Params& p, int G) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // Two tokens per warp at a time, all of a lane's partials loaded before any merge, so the
+  // merge costs a few memory round trips instead of one per partial.
+  constexpr int PER = 5;                      // 160 CTAs per pass
+  for (int m0 = warp; m0 < p.M; m0 += 2 * nwarps) {
+    const int mm[2] = {m0, m0 + nwarps};
+    b200::RowStat r[2];
+    b200::rowstat_init(r[0]);
+    b200::rowstat_init(r[1]);
+    for (int cb = 0; cb < G; cb += 32 * PER) {
+      float a[2][PER][3];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int c = cb + lane + 32 * i;
+          if (c < G && mm[t] < p.M) {
+            const float* src = p.partial + ((long long)mm[t] * G + c) * 3;
+            a[t][i][0] = __ldcg(src);
+            a[t][i][1] = __ldcg(src + 1);
+            a[t][i][2] = __ldcg(src + 2);
+          } else {
+            a[t][i][0] = -INFINITY;
+            a[t][i][1] = __int_as_float(0x7fffffff);
+            a[t][i][2] = 0.f;
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          b200::RowStat o;
+          o.m = a[t][i][0];
+          o.idx = __float_as_int(a[t][i][1]);
+          o.s = a[t][i][2];
+          r[t] = b200::rowstat_merge(r[t], o);
+        }
+      }
     }
 #pragma unroll
-    for (int msk = 1; msk < 32; msk <<= 1) r = b200::rowstat_merge(r, b200::rowstat_shfl_xor(r, msk));
-    if (lane == 0) {
-      if (p.row_max) p.row_max[m] = r.m;
-      if (p.row_arg) p.row_arg[m] = r.idx;
-      if (p.row_lse) p.row_lse[m] = r.m + logf(r.s);
+    for (int t = 0; t < 2; ++t) {
+#pragma unroll
+      for (int msk = 1; msk < 32; msk <<= 1) r[t] = b200::rowstat_merge(r[t], b200::rowstat_shfl_xor(r[t], msk));
+      if (lane == 0 && mm[t] < p.M) {
+        const int m = mm[t];
+        if (p.row_max) p.row_max[m] = r[t].m;
+        if (p.row_arg) p.row_arg[m] = r[t].idx;
+        if (p.row_lse) p.row_lse[m] = r[t].m + logf(r[t].s);
+      }
     }
   }
-  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
 }
 
 // ---- the kernel ------------------------------------------------------------------------------
@@ -503,22 +554,40 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 // (A, 128 x 128 K, shared memory) x X tile (B, T x 128 K). A 128x128 weight tile is exactly one
 // block-scale block, so every tile gets its own TMEM accumulator and the two scales are applied
 // in fp32 when the epilogue reads it back:  y[n, t] += ws[n/128, kb] * xs[t, kb] * D_kb[n, t].
-//   warp 0 (1 lane): bulk-async copies of each stage = 8 strip chunks of 2 KB (the 128-row
-//                    tile, landing in the 128-byte-swizzled K-major layout the descriptor names)
-//                    + the activation tile of that 128-K block (T x 128 B, pre-tiled);
-//   warp 1 (1 lane): TMEM allocation, then 4 tcgen05.mma kind::f8f6f4 (K = 32 each) per stage,
-//                    committed to the stage's empty barrier and the accumulator's full barrier;
-//   warps 2-5      : tcgen05.ld of their 32 TMEM lanes, fp32 scale-accumulate, and per 128-row
+//   warp 0 (1 lane): per stage ONE tensor-map copy of KW consecutive 128x128 weight tiles of a
+//                    128-row block (a 4-D box over (byte, row, strip, kb), landing as KW
+//                    [128 rows][128 B] tiles in the 128-byte-swizzled K-major layout) and ONE
+//                    bulk copy of the KW activation tiles (T x 128 B each, pre-tiled). Few large
+//                    copies per stage matter: the copy engine's cost is per operation, and
+//                    4-8 KB copies stream at about half the rate of 32 KB ones;
+//   warps 1-2      : (warp 1 also allocates TMEM) one lane each issues the 4 tcgen05.mma
+//                    kind::f8f6f4 (K = 32 each) of alternate 128-K blocks into the next TMEM
+//                    accumulator, committed to that accumulator's full barrier, and per stage
+//                    one commit to the stage's empty barrier. One thread issues an MMA about
+//                    every 120 ns whatever N is, which alone would cap the weight stream near
+//                    34 GB/s per SM; two issuers double that;
+//   warps 3-6      : tcgen05.ld of their 32 TMEM lanes, fp32 scale-accumulate, and per 128-row
 //                    block the bf16 logits and the (max, argmax, sum exp) update.
 // TMEM holds 512 / T accumulators, so the MMA warp runs ahead of the epilogue by that many
 // 128-K blocks. The activation is quantized once per call by act_tiles_kernel into the
 // workspace, already swizzled, so every stage fetches it with one copy from L2.
+//
+// Work split (stream-K): a unit is one stage (KW 128-K blocks of one 128-row block); CTA c
+// takes the contiguous units [U c / G, U (c+1) / G) of all U = nblk * K/(128 KW), so no CTA
+// does more than one unit above the mean (whole blocks per CTA would run 1187 blocks on 148
+// SMs as 9 against 8, and a 149-block vocabulary shard as 2 against 1). A CTA writes its fp32
+// partial [128 rows][T] of a block it shares with others, and per token its (max, argmax,
+// sum exp) over the blocks it finished; tc_finish_kernel (the programmatic dependent, same
+// grid) sums each shared block's partials in CTA order, writes that block and merges the row
+// statistics. No CTA waits for another, and no fence or atomic sits on the streaming path.
 
-constexpr int TC_THREADS = 192;
+constexpr int TC_ISSUERS = 2;                      // MMA-issuing warps
+constexpr int TC_THREADS = 32 * (1 + TC_ISSUERS + 4);
 constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_MAX_BUF = 16;
 constexpr int TC_TILE_W = 128 * 128;
-constexpr int TC_HDR = 512;                         // barriers, TMEM slot, flag
+constexpr int TC_HDR = 512;                         // barriers, TMEM slot, flags
+constexpr int TC_MAX_GRID = 160;                    // partial-accumulator slots are sized for it
 constexpr int TC_RED = 4 * 64 * 12;                 // [4 warps][64 tokens] RowStat
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -583,6 +652,14 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[TPAD]) {
 
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The registers a tcgen05.ld writes are valid only after tcgen05.wait::ld; passing each value
+// through an empty volatile asm placed after the wait keeps the compiler from using it earlier.
+template <int N>
+__device__ __forceinline__ void tmem_values_after_wait(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
 }
 
 // x (bf16 [M, K]) -> per-token group-128 quant, written as tiles qt[kb][tpad rows][128 B] in the
@@ -668,6 +745,81 @@ __global__ void __launch_bounds__(128)
   if (hl == 0) sr[m * KB + kb] = sc;
 }
 
+// Units of one CTA: F whole blocks (c*F ...), then leftover units [lu0, lu1) of the blocks
+// from lb0 = G*F on. A unit is (128-row block, stage j of KBS along K). The kernel uses F = 0
+// (every block is "leftover": plain stream-K, every CTA within one unit of the mean), so a
+// block is split between at most a few neighbouring CTAs and the one finishing it reads one
+// or two partials; F > 0 is kept for callers that want whole blocks first.
+struct TcWork {
+  int F, KBS, G, c, lb0;
+  long long LU, lu0, lu1;
+  __device__ int total() const { return F * KBS + (int)(lu1 - lu0); }
+  __device__ void unit(int i, int& blk, int& j) const {
+    if (i < F * KBS) {
+      blk = c * F + i / KBS;
+      j = i % KBS;
+    } else {
+      const long long lu = lu0 + (i - F * KBS);
+      blk = lb0 + (int)(lu / KBS);
+      j = (int)(lu % KBS);
+    }
+  }
+  // CTA that processes leftover unit lu (the largest c with LU*c/G <= lu).
+  __device__ int owner(long long lu) const { return (int)(((lu + 1) * G - 1) / LU); }
+  // Partial slot of CTA cc for leftover block b: 0 if b is the first block of cc's leftover run.
+  __device__ int slot(int cc, int b) const {
+    const long long l0 = LU * cc / G;
+    return (cc * 2 + ((b == lb0 + (int)(l0 / KBS)) ? 0 : 1));
+  }
+};
+
+__device__ __forceinline__ TcWork tc_work(int nblk, int KBS, int G, int c) {
+  TcWork w;
+  w.G = G;
+  w.c = c;
+  w.KBS = KBS;
+  w.F = 0;
+  w.lb0 = w.G * w.F;
+  w.LU = (long long)(nblk - w.lb0) * KBS;
+  w.lu0 = w.LU * w.c / w.G;
+  w.lu1 = w.LU * (w.c + 1) / w.G;
+  return w;
+}
+
+// Output of one finished 128-row block held as acc[T] for row 32*qd + lane, through a [32][33]
+// shared tile `tr` of this warp: lanes hold rows on the way in and tokens on the way out, so
+// each lane stores 32 consecutive logits of one token (64 contiguous bytes) and folds that
+// token's (max, argmax, sum exp) over its 32 rows into st in one merge.
+template <int TPAD, bool STATS>
+__device__ __forceinline__ void tc_block_out(const Params& p, const float (&acc)[TPAD], int blk, int qd, int lane,
+                                             float* tr, b200::RowStat (&st)[TPAD / 32]) {
+  const int n0 = blk * 128 + 32 * qd;
+#pragma unroll
+  for (int c = 0; c < TPAD / 32; ++c) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tr[j * 33 + lane] = acc[32 * c + j];
+    __syncwarp();
+    const int t = 32 * c + lane;
+    if (t < p.M) {
+      float v[32];
+#pragma unroll
+      for (int r = 0; r < 32; ++r) v[r] = tr[lane * 33 + r];
+      if (p.y != nullptr) {
+        uint4* dst = reinterpret_cast<uint4*>(p.y + (long long)t * p.ldy + n0);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          __nv_bfloat162 h[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[8 * q4 + 2 * i], v[8 * q4 + 2 * i + 1]);
+          dst[q4] = *reinterpret_cast<const uint4*>(h);
+        }
+      }
+      if (STATS) b200::rowstat_push32(st[c], v, (int)(n0 + p.vocab_offset));
+    }
+    __syncwarp();
+  }
+}
+
 template <int TPAD, bool STATS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     fp8_tc_kernel(const __grid_constant__ CUtensorMap wmap, Params p, const uint8_t* __restrict__ qt,
@@ -676,13 +828,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t raw = b200::smem_u32(sm_raw);
   char* sm = sm_raw + ((1024u - (raw & 1023u)) & 1023u);
   constexpr int XT_BYTES = TPAD * 128;
-  constexpr int STAGE = TC_TILE_W + XT_BYTES;
+  const int KW = p.kw;
+  const int STAGE = KW * (TC_TILE_W + XT_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = p.K / 128;
-  const int nblk = p.N / 128;
-  const int b0 = (int)(((long long)blockIdx.x * nblk) / gridDim.x);
-  const int b1 = (int)(((long long)(blockIdx.x + 1) * nblk) / gridDim.x);
-  const int total = (b1 - b0) * KB;
+  const TcWork wk = tc_work(p.N / 128, KB / KW, gridDim.x, blockIdx.x);
+  const int total = wk.total();
   const int nstage = p.nstage, nbuf = p.kps;          // kps carries the accumulator count here
 
   uint64_t* w_full = reinterpret_cast<uint64_t*>(sm);
@@ -692,22 +843,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* xs_bar = a_empty + TC_MAX_BUF;
   uint64_t* done_bar = xs_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-  int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
   b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + TC_HDR);
   float* xs_s = reinterpret_cast<float*>(sm + p.xs_off);       // [KB][TPAD]
   char* ring = sm + p.ring_off;
 
   if (threadIdx.x == 0) {
+    // KW is 1 or a multiple of TC_ISSUERS, so a stage's 128-K blocks go to min(KW, issuers)
+    // distinct issuers, each committing once to the stage's empty barrier.
+    const int issuers_per_stage = KW < TC_ISSUERS ? KW : TC_ISSUERS;
     for (int i = 0; i < nstage; ++i) {
       b200::mbar_init(&w_full[i], 1);
-      b200::mbar_init(&w_empty[i], 1);
+      b200::mbar_init(&w_empty[i], issuers_per_stage);
     }
     for (int i = 0; i < nbuf; ++i) {
       b200::mbar_init(&a_full[i], 1);
       b200::mbar_init(&a_empty[i], 4);
     }
     b200::mbar_init(xs_bar, 1);
-    b200::mbar_init(done_bar, 1);
+    b200::mbar_init(done_bar, TC_ISSUERS);
     b200::fence_mbar_init();
   }
   if (warp == 1) {
@@ -721,29 +874,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint64_t deadline = b200::globaltimer_ns() + WAIT_NS;
+  griddep_launch_dependents();              // tc_finish_kernel may be scheduled as SMs free up
 
   if (warp == 0) {
     // ---------------- producer ----------------
     // Weight tiles do not depend on the activation kernel (this grid's programmatic primary),
     // so the first ring of weight tiles is issued before griddepcontrol.wait; each stage's
-    // activation tile (and the scales) only after it.
+    // activation tiles (and the scales) only after it.
     if (lane == 0) {
       const uint64_t pol = b200::l2_policy_evict_first();
       const uint64_t wmap_addr = reinterpret_cast<uint64_t>(&wmap);
       auto issue_w = [&](int it) {
         const int s = it % nstage;
-        const int blk = b0 + it / KB, kb = it % KB;
+        int blk, j;
+        wk.unit(it, blk, j);
         b200::mbar_arrive_expect_tx(&w_full[s], STAGE);
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
             " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(b200::smem_u32(ring + s * STAGE)),
-            "l"(wmap_addr), "r"(0), "r"(0), "r"(kb), "r"(blk * 8), "r"(b200::smem_u32(&w_full[s])),
+            "l"(wmap_addr), "r"(0), "r"(0), "r"(blk * 8), "r"(j * KW), "r"(b200::smem_u32(&w_full[s])),
             "l"(pol)
             : "memory");
       };
       auto issue_x = [&](int it) {
-        const int s = it % nstage, kb = it % KB;
-        b200::bulk_g2s(ring + s * STAGE + TC_TILE_W, qt + (long long)kb * XT_BYTES, XT_BYTES, &w_full[s]);
+        const int s = it % nstage;
+        int blk, j;
+        wk.unit(it, blk, j);
+        b200::bulk_g2s(ring + s * STAGE + KW * TC_TILE_W, qt + (long long)j * KW * XT_BYTES,
+                       KW * XT_BYTES, &w_full[s]);
       };
       const int first = min(nstage, total);
       for (int it = 0; it < first; ++it) issue_w(it);
@@ -769,28 +927,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       b200::mbar_wait_bounded(xs_bar, 0, deadline + WAIT_NS);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp <= TC_ISSUERS) {
+    // ---------------- MMA issuers: 128-K block number kbit goes to issuer kbit % TC_ISSUERS ----
     if (lane == 0) {
+      const int me = warp - 1;
       const uint32_t idesc = (1u << 4)                        // D: f32
                              | ((uint32_t)(TPAD >> 3) << 17)  // N
                              | ((uint32_t)(128 >> 4) << 24);  // M = 128; A, B e4m3, K-major
       bool ok = true;
-      for (int it = 0; it < total; ++it) {
-        const int s = it % nstage, buf = it % nbuf;
+      for (int it = 0; it < total && ok; ++it) {
+        const int s = it % nstage;
+        if (KW < TC_ISSUERS && (it * KW) % TC_ISSUERS != me) continue;     // not my stage
         if (!b200::mbar_wait_bounded(&w_full[s], (it / nstage) & 1, deadline)) { ok = false; break; }
-        if (it >= nbuf && !b200::mbar_wait_bounded(&a_empty[buf], ((it / nbuf) - 1) & 1, deadline)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const uint32_t st = b200::smem_u32(ring + s * STAGE);
-        const uint64_t ad = sw128_desc(st), bd = sw128_desc(st + TC_TILE_W);
-        const uint32_t d = tmem + (uint32_t)(buf * TPAD);
+        for (int q = 0; q < KW; ++q) {
+          const int kbit = it * KW + q;
+          if (kbit % TC_ISSUERS != me) continue;
+          const int buf = kbit % nbuf;
+          if (kbit >= nbuf && !b200::mbar_wait_bounded(&a_empty[buf], ((kbit / nbuf) - 1) & 1, deadline)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(st + q * TC_TILE_W);
+          const uint64_t bd = sw128_desc(st + KW * TC_TILE_W + q * XT_BYTES);
+          const uint32_t d = tmem + (uint32_t)(buf * TPAD);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma_f8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) tc_mma_f8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
+          tc_commit(&a_full[buf]);
+        }
         tc_commit(&w_empty[s]);
-        tc_commit(&a_full[buf]);
       }
       if (!ok) atomicExch(&g_lmhead_err, 1);
       tc_commit(done_bar);                                     // every issued MMA has landed
@@ -799,79 +965,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue ----------------
+    // After a timed-out wait the warps carry on without touching TMEM (so every warp still
+    // reaches the final barrier) and the error word reports the call.
     const int qd = warp & 3;                  // TMEM lane quarter this warp may access
-    const int ew = warp - 2;
+    const int ew = warp - 1 - TC_ISSUERS;
+    const int row = 32 * qd + lane;           // row of the 128-row block held by this lane
     b200::RowStat st[TPAD / 32];
 #pragma unroll
     for (int i = 0; i < TPAD / 32; ++i) b200::rowstat_init(st[i]);
     bool ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xs_bar, 0, deadline));
-    int it = 0;
-    for (int blk = b0; blk < b1 && ok; ++blk) {
+    int kbit = 0;
+    for (int it = 0; it < total;) {
+      int blk, j0;
+      wk.unit(it, blk, j0);
       float acc[TPAD];
 #pragma unroll
       for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
       const float* wsrow = static_cast<const float*>(p.wscale) + (long long)blk * KB;
       const float wsv = (lane < KB) ? __ldg(wsrow + lane) : 0.f;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int buf = it % nbuf;
-        const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb) : __ldg(wsrow + kb);
-        if (!__all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (it / nbuf) & 1, deadline))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
-        float v[TPAD];
-        tmem_ld_row<TPAD>(ta, v);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
-        const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
+      int j1 = j0;
+      for (;; ++it) {
+        int b2, jj;
+        if (it >= total) break;
+        wk.unit(it, b2, jj);
+        if (b2 != blk) break;
+        j1 = jj;
+        for (int q = 0; q < KW; ++q, ++kbit) {
+          const int kb = jj * KW + q, buf = kbit % nbuf;
+          const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb & 31) : __ldg(wsrow + kb);
+          if (ok) ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (kbit / nbuf) & 1, deadline));
+          if (!ok) continue;
+          tc_fence_after();
+          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
+          float v[TPAD];
+          tmem_ld_row<TPAD>(ta, v);
+          tmem_wait_ld();
+          tmem_values_after_wait(v);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
+          const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
 #pragma unroll
-        for (int j = 0; j < TPAD; j += 4) {
-          const float4 xv = xs4[j >> 2];
-          acc[j] = fmaf(v[j], sw * xv.x, acc[j]);
-          acc[j + 1] = fmaf(v[j + 1], sw * xv.y, acc[j + 1]);
-          acc[j + 2] = fmaf(v[j + 2], sw * xv.z, acc[j + 2]);
-          acc[j + 3] = fmaf(v[j + 3], sw * xv.w, acc[j + 3]);
-        }
-      }
-      if (!ok) break;
-      // Block epilogue through a per-warp [32][33] shared tile: lanes hold rows on the way in
-      // and tokens on the way out, so each lane stores 32 consecutive logits of one token
-      // (64 contiguous bytes) and updates that token's (max, argmax, sum exp) over its 32
-      // rows in increasing row order -- no cross-lane reduction per token.
-      float* tr = reinterpret_cast<float*>(sm + p.x_off) + ew * (32 * 33);
-      const int n0 = blk * 128 + 32 * qd;
-#pragma unroll
-      for (int c = 0; c < TPAD / 32; ++c) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tr[j * 33 + lane] = acc[32 * c + j];
-        __syncwarp();
-        const int t = 32 * c + lane;
-        if (t < p.M) {
-          float v[32];
-#pragma unroll
-          for (int r = 0; r < 32; ++r) v[r] = tr[lane * 33 + r];
-          if (p.y != nullptr) {
-            uint4* dst = reinterpret_cast<uint4*>(p.y + (long long)t * p.ldy + n0);
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              __nv_bfloat162 h[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[8 * q4 + 2 * i], v[8 * q4 + 2 * i + 1]);
-              dst[q4] = *reinterpret_cast<const uint4*>(h);
-            }
-          }
-          if (STATS) {
-            const int base = (int)(n0 + p.vocab_offset);
-#pragma unroll
-            for (int r = 0; r < 32; ++r) b200::rowstat_push(st[c], v[r], base + r);
+          for (int j = 0; j < TPAD; j += 4) {
+            const float4 xv = xs4[j >> 2];
+            acc[j] = fmaf(v[j], sw * xv.x, acc[j]);
+            acc[j + 1] = fmaf(v[j + 1], sw * xv.y, acc[j + 1]);
+            acc[j + 2] = fmaf(v[j + 2], sw * xv.z, acc[j + 2]);
+            acc[j + 3] = fmaf(v[j + 3], sw * xv.w, acc[j + 3]);
           }
         }
-        __syncwarp();
       }
+      if (j0 != 0 || j1 != wk.KBS - 1) {
+        // A block shared with other CTAs: publish this CTA's fp32 partial; tc_finish_kernel
+        // sums the partials in CTA order and writes the block.
+        float4* dst = reinterpret_cast<float4*>(p.px + ((long long)wk.slot(wk.c, blk) * 128 + row) * TPAD);
+#pragma unroll
+        for (int j = 0; j < TPAD; j += 4) dst[j >> 2] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        continue;
+      }
+      tc_block_out<TPAD, STATS>(p, acc, blk, qd, lane, reinterpret_cast<float*>(sm + p.x_off) + ew * (32 * 33), st);
     }
     if (!ok) atomicExch(&g_lmhead_err, 1);
     if (STATS) {
@@ -885,7 +1037,128 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
   }
-  if (STATS) stats_finalize(p, red, 64, 4, s_flag);
+  if (STATS) stats_write_partial(p, red, 64, 4, blockIdx.x, 2 * gridDim.x);
+}
+
+// Completes the 128-row blocks fp8_tc_kernel split between CTAs: sums their fp32 partials in
+// CTA order, writes the block like the main kernel and puts its row statistics in partial
+// slot G + blockIdx.x (next to the main grid's G slots). Launched as the programmatic
+// dependent of fp8_tc_kernel with the same grid size G; 128 threads, thread = block row.
+template <int TPAD, bool STATS>
+__global__ void __launch_bounds__(128) tc_finish_kernel(Params p, int KBS) {
+  __shared__ float tr_all[4][32 * 33];
+  __shared__ b200::RowStat red[4 * 64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = threadIdx.x;
+  const int G = gridDim.x, nblk = p.N / 128;
+  const TcWork wk = tc_work(nblk, KBS, G, 0);
+  b200::RowStat st[TPAD / 32];
+#pragma unroll
+  for (int i = 0; i < TPAD / 32; ++i) b200::rowstat_init(st[i]);
+  griddep_launch_dependents();              // stats_merge_kernel may be scheduled
+  griddep_wait();                           // the main grid has finished; its writes are visible
+  // CTA c finishes the block in which main-grid CTA c's units start, when that start is inside
+  // a block whose first unit belongs to CTA c - 1: every split block has exactly one such c.
+  const int c = blockIdx.x;
+  const long long lu_c = wk.LU * c / G;
+  if (c > 0 && lu_c % KBS != 0 && wk.owner(lu_c / KBS * KBS) == c - 1) {
+    const int b = (int)(lu_c / KBS);
+    const long long u0 = (long long)b * KBS;
+    float acc[TPAD];
+#pragma unroll
+    for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
+    int prev = -1;
+    for (int u = 0; u < KBS; ++u) {
+      const int cc = wk.owner(u0 + u);
+      if (cc == prev) continue;
+      prev = cc;
+      const float4* src = reinterpret_cast<const float4*>(p.px + ((long long)wk.slot(cc, b) * 128 + row) * TPAD);
+      float4 v4[TPAD / 4];
+#pragma unroll
+      for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j);
+#pragma unroll
+      for (int j = 0; j < TPAD / 4; ++j) {
+        acc[4 * j] += v4[j].x;
+        acc[4 * j + 1] += v4[j].y;
+        acc[4 * j + 2] += v4[j].z;
+        acc[4 * j + 3] += v4[j].w;
+      }
+    }
+    tc_block_out<TPAD, STATS>(p, acc, b, warp, lane, tr_all[warp], st);
+  }
+  if constexpr (STATS) {
+#pragma unroll
+    for (int i = 0; i < TPAD / 32; ++i) red[warp * 64 + 32 * i + lane] = st[i];
+    __syncthreads();
+    stats_write_partial(p, red, 64, 4, G + blockIdx.x, 2 * G);
+  }
+}
+
+// Final (max, first argmax, logsumexp) of token blockIdx.x from its `nslots` partials: the max
+// and the smallest index attaining it first, then sum_i s_i exp(m_i - max) as independent terms
+// (no chain of rescalings), each in a fixed reduction order. 256 threads; the programmatic
+// dependent of tc_finish_kernel.
+__global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) {
+  __shared__ float s_m[8];
+  __shared__ int s_i[8];
+  __shared__ float s_s[8];
+  const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_wait();
+  const float* base = p.partial + (long long)m * nslots * 3;
+  float pm[2], ps[2];
+  int pi[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    const bool v = i < nslots;
+    pm[k] = v ? __ldcg(base + 3 * i) : -INFINITY;
+    pi[k] = v ? __float_as_int(__ldcg(base + 3 * i + 1)) : 0x7fffffff;
+    ps[k] = v ? __ldcg(base + 3 * i + 2) : 0.f;
+  }
+  for (int i = threadIdx.x + 512; i < nslots; i += 256) {      // more than 512 slots: fold in
+    const float mm = __ldcg(base + 3 * i), ss = __ldcg(base + 3 * i + 2);
+    const int ii = __float_as_int(__ldcg(base + 3 * i + 1));
+    b200::RowStat a{pm[1], pi[1], ps[1]}, b{mm, ii, ss};
+    a = b200::rowstat_merge(a, b);
+    pm[1] = a.m; pi[1] = a.idx; ps[1] = a.s;
+  }
+  // max and first index at it
+  float mx = fmaxf(pm[0], pm[1]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_m[warp] = mx;
+  __syncthreads();
+  mx = s_m[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_m[w]);
+  int id = 0x7fffffff;
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    if (pm[k] == mx && ps[k] > 0.f) id = min(id, pi[k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) id = min(id, __shfl_xor_sync(0xffffffffu, id, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    if (ps[k] > 0.f) sum += ps[k] * expf(pm[k] - mx);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) {
+    s_i[warp] = id;
+    s_s[warp] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    int best = 0x7fffffff;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      t += s_s[w];
+      best = min(best, s_i[w]);
+    }
+    if (p.row_max) p.row_max[m] = mx;
+    if (p.row_arg) p.row_arg[m] = best;
+    if (p.row_lse) p.row_lse[m] = mx + logf(t);
+  }
 }
 
 // ---- read-only stream control (hcq_stream_probe, hcq_fp8skinny.hip:206-224) -----------------
@@ -980,33 +1253,45 @@ int launch_m(const Params& p, cudaStream_t stream) {
 
 // Workspace: [0,16) ticket counter | [16, 16+1024*64*12) per-CTA row statistics |
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
-// [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales.
+// [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
+// [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 blocks split between CTAs, two
+// [128][64] slots per CTA.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
 constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
 constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
-constexpr long long WORKSPACE_BYTES = SR_OFF + SR_CAP;
+constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 2LL * TC_MAX_GRID * 128 * 64 * 4;
+constexpr long long WORKSPACE_BYTES = PX_OFF + PX_CAP;
 static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
 
+// Shared-memory plan of the tcgen05 kernel: the widest stage (KW 128-K blocks, KW | K/128)
+// that still leaves at least 3 stages in the ring. Returns the dynamic smem bytes or -1.
 int plan_tc(Params& p, int tpad) {
   const int KB = p.K / 128;
   p.xs_off = TC_HDR + TC_RED;
   p.x_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;          // 4 warps x [32][33] fp32 tiles
   p.ring_off = (p.x_off + 4 * 32 * 33 * 4 + 1023) & ~1023;
-  const int stage = TC_TILE_W + tpad * 128;
   const int avail = SMEM_CAP - 1024 - p.ring_off;
-  const int nstage = min(TC_MAX_STAGES, avail / stage);
-  if (nstage < 2) return -1;
-  p.nstage = nstage;
-  p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
-  return 1024 + p.ring_off + nstage * stage;
+  for (int kw = 4; kw >= 1; kw >>= 1) {
+    if (KB % kw) continue;
+    const int stage = kw * (TC_TILE_W + tpad * 128);
+    const int nstage = min(TC_MAX_STAGES, avail / stage);
+    if (nstage >= 3 || (kw == 1 && nstage >= 2)) {
+      p.kw = kw;
+      p.nstage = nstage;
+      p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
+      return 1024 + p.ring_off + nstage * stage;
+    }
+  }
+  return -1;
 }
 
-// 4-D view of the strip-packed weight for the tensor-map copy: (byte 128, row 16, kb, strip);
-// one (128, 16, 1, 8) box = the 128-row x 128-K tile, landing as [128 rows][128 B] already in
-// the 128-byte-swizzled order (the pack stores it that way, so the copy itself does not swizzle).
-int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
+// 4-D view of the strip-packed weight for the tensor-map copy: (byte 128, row 16, strip, kb),
+// the strip and kb strides swapped against memory order so that one (128, 16, 8, kw) box is
+// kw consecutive 128x128 tiles of one 128-row block, each landing as [128 rows][128 B] already
+// in the 128-byte-swizzled order (the pack stores it that way; the copy itself does not swizzle).
+int make_strip_map(CUtensorMap* m, const void* w, int N, int K, int kw) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -1017,9 +1302,9 @@ int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
   const int KB = K / 128;
-  cuuint64_t dims[4] = {128, 16, (cuuint64_t)KB, (cuuint64_t)(N / 16)};
-  cuuint64_t strides[3] = {128, 2048, (cuuint64_t)KB * 2048};
-  cuuint32_t box[4] = {128, 16, 1, 8};
+  cuuint64_t dims[4] = {128, 16, (cuuint64_t)(N / 16), (cuuint64_t)KB};
+  cuuint64_t strides[3] = {128, (cuuint64_t)KB * 2048, 2048};
+  cuuint32_t box[4] = {128, 16, 8, (cuuint32_t)kw};
   cuuint32_t es[4] = {1, 1, 1, 1};
   const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(w), dims, strides, box,
                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1033,23 +1318,29 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   if ((long long)KB * TPAD * 128 > QT_CAP || (long long)TPAD * KB * 4 > XT_CAP) return -8;
   if ((reinterpret_cast<uintptr_t>(p.w) & 127) != 0) return -10;
   if (p.y != nullptr && ((p.ldy % 8) != 0 || (reinterpret_cast<uintptr_t>(p.y) & 15) != 0)) return -10;
+  const int smem = plan_tc(p, TPAD);
+  if (smem < 0) return -8;
   CUtensorMap wmap;
-  if (make_strip_map(&wmap, p.w, p.N, p.K) != 0) return -12;
+  if (make_strip_map(&wmap, p.w, p.N, p.K, p.kw) != 0) return -12;
   char* base = reinterpret_cast<char*>(p.counter);
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
+  p.px = reinterpret_cast<float*>(base + PX_OFF);
   int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,
                      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M,
                      p.K, TPAD, qt, xt, p.qx_out, p.xs_out);
   if (rc != 0) return rc;
-  const int smem = plan_tc(p, TPAD);
-  if (smem < 0) return -8;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
   cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   p.pdl = 1;
-  const int grid = min(p.N / 128, num_sms());
-  return launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
+  const long long units = (long long)(p.N / 128) * (KB / p.kw);
+  const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
+  rc = launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
+  if (rc != 0) return rc;
+  rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(128), 0, stream, true, p, KB / p.kw);
+  if (rc != 0 || !STATS) return rc;
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, 2 * grid);
 }
 
 template <bool STATS>
@@ -1261,7 +1552,7 @@ int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
 // b200_fp8_lmhead needs a caller-owned workspace. Some callers cannot hand one over: a plain C
 // or ctypes binding that has no device allocator of its own, or code running where an
 // allocation is not allowed (a caching allocator's hook, a memory-capped pool). For those the
-// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 2.4 MB per
+// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 12.3 MB per
 // device, reserved when the library's device code is loaded).
 
 namespace {
