@@ -554,41 +554,46 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 // (A, 128 x 128 K, shared memory) x X tile (B, T x 128 K). A 128x128 weight tile is exactly one
 // block-scale block, so every tile gets its own TMEM accumulator and the two scales are applied
 // in fp32 when the epilogue reads it back:  y[n, t] += ws[n/128, kb] * xs[t, kb] * D_kb[n, t].
-//   warp 0 (1 lane): per stage ONE tensor-map copy of KW consecutive 128x128 weight tiles of a
-//                    128-row block (a 4-D box over (byte, row, strip, kb), landing as KW
-//                    [128 rows][128 B] tiles in the 128-byte-swizzled K-major layout) and ONE
-//                    bulk copy of the KW activation tiles (T x 128 B each, pre-tiled). Few large
-//                    copies per stage matter: the copy engine's cost is per operation, and
-//                    4-8 KB copies stream at about half the rate of 32 KB ones;
-//   warps 1-2      : (warp 1 also allocates TMEM) one lane each issues the 4 tcgen05.mma
-//                    kind::f8f6f4 (K = 32 each) of alternate 128-K blocks into the next TMEM
-//                    accumulator, committed to that accumulator's full barrier, and per stage
-//                    one commit to the stage's empty barrier. One thread issues an MMA about
-//                    every 120 ns whatever N is, which alone would cap the weight stream near
-//                    34 GB/s per SM; two issuers double that;
-//   warps 3-6      : tcgen05.ld of their 32 TMEM lanes, fp32 scale-accumulate, and per 128-row
-//                    block the bf16 logits and the (max, argmax, sum exp) update.
-// TMEM holds 512 / T accumulators, so the MMA warp runs ahead of the epilogue by that many
-// 128-K blocks. The activation is quantized once per call by act_tiles_kernel into the
-// workspace, already swizzled, so every stage fetches it with one copy from L2.
 //
-// Work split (stream-K): a unit is one stage (KW 128-K blocks of one 128-row block); CTA c
-// takes the contiguous units [U c / G, U (c+1) / G) of all U = nblk * K/(128 KW), so no CTA
-// does more than one unit above the mean (whole blocks per CTA would run 1187 blocks on 148
-// SMs as 9 against 8, and a 149-block vocabulary shard as 2 against 1). A CTA writes its fp32
-// partial [128 rows][T] of a block it shares with others, and per token its (max, argmax,
-// sum exp) over the blocks it finished; tc_finish_kernel (the programmatic dependent, same
-// grid) sums each shared block's partials in CTA order, writes that block and merges the row
-// statistics. No CTA waits for another, and no fence or atomic sits on the streaming path.
+// The weight stream has to keep about 170 KB in flight per SM (loaded-HBM latency is 3-4 us),
+// while a stage is held about 1 us after it lands (its MMAs run about 85 ns each whatever T
+// is). So a stage carries the two 128-row blocks of a block PAIR at one 128-K block -- one
+// 32 KB tensor-map copy, a (byte, row, strip, kb) box of 16 strips landing as two swizzled
+// [128 rows][128 B] tiles -- and ONE activation tile both use; five such stages fit.
+//   warp 0 (1 lane): the two copies of each stage (weights; T x 128 B pre-tiled activation);
+//   warps 1-2      : (warp 1 also allocates TMEM) lane 0 of warp 1 + s issues the 4
+//                    tcgen05.mma kind::f8f6f4 (K = 32 each) of block 2p + s into its next TMEM
+//                    accumulator and commits it; both commit each stage's empty barrier. A
+//                    thread issues an MMA only every ~120 ns, so one issuer per block matters;
+//   warps 3-10     : two groups of four (group s = block 2p + s; warp & 3 = TMEM lane
+//                    quarter): tcgen05.ld of the accumulator, fp32 scale-accumulate in
+//                    registers, and per finished block the bf16 logits (lane = row: each token
+//                    is one coalesced 64-byte store per warp) and per token the (max, first
+//                    argmax, sum exp) by warp reductions.
+// TMEM holds 512 / T accumulators, so the MMAs run ahead of the epilogue by 256 / T stages.
+// The activation is quantized once per call by act_tiles_kernel into the workspace, already
+// swizzled.
+//
+// Work split (stream-K): a unit is one stage (block pair, 128-K block); CTA c takes the
+// contiguous units [U c / G, U (c+1) / G) of all U = ceil(nblk/2) * K/128, so no CTA does more
+// than one unit above the mean (whole blocks per CTA would run 1187 blocks on 148 SMs as 9
+// against 8, and a 149-block vocabulary shard as 2 against 1). A CTA writes its fp32 partial
+// [128 rows][T] of each block of a pair it shares with other CTAs, and per token its (max,
+// argmax, sum exp) over the blocks it finished; tc_finish_kernel (the programmatic dependent,
+// same grid) sums each shared pair's partials in CTA order and writes those blocks, and
+// stats_merge_kernel merges the row statistics. No CTA waits for another, and no fence or
+// atomic sits on the streaming path. With an odd block count the last pair's second block
+// lies beyond the tensor: the copy fills it with zeros and nothing of it is written.
 
-constexpr int TC_ISSUERS = 2;                      // MMA-issuing warps
-constexpr int TC_THREADS = 32 * (1 + TC_ISSUERS + 4);
+constexpr int TC_ISSUERS = 2;                       // MMA-issuing warps, one per block of a pair
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_THREADS = 32 * (1 + TC_ISSUERS + TC_EPI_WARPS);
 constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_MAX_BUF = 16;
 constexpr int TC_TILE_W = 128 * 128;
-constexpr int TC_HDR = 512;                         // barriers, TMEM slot, flags
+constexpr int TC_PAIR_W = 2 * TC_TILE_W;
+constexpr int TC_HDR = 512;                         // barriers, TMEM slot
 constexpr int TC_MAX_GRID = 160;                    // partial-accumulator slots are sized for it
-constexpr int TC_RED = 4 * 64 * 12;                 // [4 warps][64 tokens] RowStat
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -746,10 +751,9 @@ __global__ void __launch_bounds__(128)
 }
 
 // Units of one CTA: F whole blocks (c*F ...), then leftover units [lu0, lu1) of the blocks
-// from lb0 = G*F on. A unit is (128-row block, stage j of KBS along K). The kernel uses F = 0
-// (every block is "leftover": plain stream-K, every CTA within one unit of the mean), so a
-// block is split between at most a few neighbouring CTAs and the one finishing it reads one
-// or two partials; F > 0 is kept for callers that want whole blocks first.
+// from lb0 = G*F on. A unit is (block, stage j of KBS along K); for the tcgen05 kernel a
+// "block" is a block pair. The kernel uses F = 0 (plain stream-K), so a pair is split
+// between at most a few neighbouring CTAs.
 struct TcWork {
   int F, KBS, G, c, lb0;
   long long LU, lu0, lu1;
@@ -764,12 +768,13 @@ struct TcWork {
       j = (int)(lu % KBS);
     }
   }
-  // CTA that processes leftover unit lu (the largest c with LU*c/G <= lu).
-  __device__ int owner(long long lu) const { return (int)(((lu + 1) * G - 1) / LU); }
+  // CTA that processes leftover unit lu (the largest c with LU*c/G <= lu). The host keeps
+  // LU * G below 2^31, so the arithmetic is 32-bit.
+  __device__ int owner(long long lu) const { return (((int)lu + 1) * G - 1) / (int)LU; }
   // Partial slot of CTA cc for leftover block b: 0 if b is the first block of cc's leftover run.
   __device__ int slot(int cc, int b) const {
-    const long long l0 = LU * cc / G;
-    return (cc * 2 + ((b == lb0 + (int)(l0 / KBS)) ? 0 : 1));
+    const int l0 = (int)LU * cc / G;
+    return (cc * 2 + ((b == lb0 + l0 / KBS) ? 0 : 1));
   }
 };
 
@@ -786,37 +791,76 @@ __device__ __forceinline__ TcWork tc_work(int nblk, int KBS, int G, int c) {
   return w;
 }
 
-// Output of one finished 128-row block held as acc[T] for row 32*qd + lane, through a [32][33]
-// shared tile `tr` of this warp: lanes hold rows on the way in and tokens on the way out, so
-// each lane stores 32 consecutive logits of one token (64 contiguous bytes) and folds that
-// token's (max, argmax, sum exp) over its 32 rows into st in one merge.
+// Output of one finished 128-row block: lane = row n0 + lane of the warp's 32 rows, acc[t] its
+// logit for token t. Sixteen tokens at a time pass through the warp's [16][33] shared tile
+// `tr`, after which lane (tt = lane & 15, rg = lane >> 4) holds rows n0 + 16 rg .. + 15 of
+// token 16 ch + tt: two 16-byte stores of bf16 logits; the max over the 32 rows, the first row
+// at it and the sum of exp(v - max) by trees over independent values and one shuffle across
+// the two row groups. Lane tt (< 16) folds token 16 ch + tt's block result into st[ch].
+constexpr int TC_CHUNK = 16;
+
 template <int TPAD, bool STATS>
-__device__ __forceinline__ void tc_block_out(const Params& p, const float (&acc)[TPAD], int blk, int qd, int lane,
-                                             float* tr, b200::RowStat (&st)[TPAD / 32]) {
-  const int n0 = blk * 128 + 32 * qd;
+__device__ __forceinline__ void tc_block_rows(const Params& p, const float (&acc)[TPAD], int n0, int lane,
+                                              float* tr, b200::RowStat (&st)[TPAD / TC_CHUNK]) {
+  const int tt = lane & 15, rg = lane >> 4;
 #pragma unroll
-  for (int c = 0; c < TPAD / 32; ++c) {
+  for (int ch = 0; ch < TPAD / TC_CHUNK; ++ch) {
+    if (TC_CHUNK * ch < p.M) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) tr[j * 33 + lane] = acc[32 * c + j];
-    __syncwarp();
-    const int t = 32 * c + lane;
-    if (t < p.M) {
-      float v[32];
+      for (int i = 0; i < TC_CHUNK; ++i) tr[i * 33 + lane] = acc[TC_CHUNK * ch + i];
+      __syncwarp();
+      float v[16];
 #pragma unroll
-      for (int r = 0; r < 32; ++r) v[r] = tr[lane * 33 + r];
-      if (p.y != nullptr) {
-        uint4* dst = reinterpret_cast<uint4*>(p.y + (long long)t * p.ldy + n0);
+      for (int r = 0; r < 16; ++r) v[r] = tr[tt * 33 + 16 * rg + r];
+      __syncwarp();
+      const int t = TC_CHUNK * ch + tt;
+      const bool live = t < p.M;
+      if (live && p.y != nullptr) {
+        __nv_bfloat162 h[8];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          __nv_bfloat162 h[4];
+        for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(p.y + (long long)t * p.ldy + n0 + 16 * rg);
+        dst[0] = *reinterpret_cast<const uint4*>(&h[0]);
+        dst[1] = *reinterpret_cast<const uint4*>(&h[4]);
+      }
+      if (STATS) {
+        float mt[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[8 * q4 + 2 * i], v[8 * q4 + 2 * i + 1]);
-          dst[q4] = *reinterpret_cast<const uint4*>(h);
+        for (int i = 0; i < 8; ++i) mt[i] = fmaxf(v[i], v[i + 8]);
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1) {
+#pragma unroll
+          for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
+        }
+        const float m = fmaxf(mt[0], __shfl_xor_sync(0xffffffffu, mt[0], 16));
+        int it[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) it[i] = (v[i] == m) ? i : ((v[i + 8] == m) ? i + 8 : 0x7fffffff);
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1) {
+#pragma unroll
+          for (int i = 0; i < w; ++i) it[i] = min(it[i], it[i + w]);
+        }
+        const int ir0 = (it[0] == 0x7fffffff) ? 0x7fffffff : 16 * rg + it[0];
+        const int ir = min(ir0, __shfl_xor_sync(0xffffffffu, ir0, 16));
+        float et[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) et[i] = __expf(v[i] - m) + __expf(v[i + 8] - m);
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1) {
+#pragma unroll
+          for (int i = 0; i < w; ++i) et[i] += et[i + w];
+        }
+        const float e = et[0] + __shfl_xor_sync(0xffffffffu, et[0], 16);
+        if (live && rg == 0) {
+          b200::RowStat b;
+          b.m = m;
+          b.idx = (int)(n0 + p.vocab_offset) + ir;
+          b.s = e;
+          st[ch] = b200::rowstat_merge(st[ch], b);
         }
       }
-      if (STATS) b200::rowstat_push32(st[c], v, (int)(n0 + p.vocab_offset));
     }
-    __syncwarp();
   }
 }
 
@@ -828,11 +872,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t raw = b200::smem_u32(sm_raw);
   char* sm = sm_raw + ((1024u - (raw & 1023u)) & 1023u);
   constexpr int XT_BYTES = TPAD * 128;
-  const int KW = p.kw;
-  const int STAGE = KW * (TC_TILE_W + XT_BYTES);
+  constexpr int STAGE = TC_PAIR_W + XT_BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = p.K / 128;
-  const TcWork wk = tc_work(p.N / 128, KB / KW, gridDim.x, blockIdx.x);
+  const int nblk = p.N / 128;
+  const TcWork wk = tc_work((nblk + 1) / 2, KB, gridDim.x, blockIdx.x);
   const int total = wk.total();
   const int nstage = p.nstage, nbuf = p.kps;          // kps carries the accumulator count here
 
@@ -843,21 +887,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* xs_bar = a_empty + TC_MAX_BUF;
   uint64_t* done_bar = xs_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-  b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + TC_HDR);
   float* xs_s = reinterpret_cast<float*>(sm + p.xs_off);       // [KB][TPAD]
   char* ring = sm + p.ring_off;
+  b200::RowStat st[TPAD / TC_CHUNK];        // epilogue lanes l < 16: tokens 16 ch + l
 
   if (threadIdx.x == 0) {
-    // KW is 1 or a multiple of TC_ISSUERS, so a stage's 128-K blocks go to min(KW, issuers)
-    // distinct issuers, each committing once to the stage's empty barrier.
-    const int issuers_per_stage = KW < TC_ISSUERS ? KW : TC_ISSUERS;
     for (int i = 0; i < nstage; ++i) {
       b200::mbar_init(&w_full[i], 1);
-      b200::mbar_init(&w_empty[i], issuers_per_stage);
+      b200::mbar_init(&w_empty[i], TC_ISSUERS);
     }
     for (int i = 0; i < nbuf; ++i) {
       b200::mbar_init(&a_full[i], 1);
-      b200::mbar_init(&a_empty[i], 4);
+      b200::mbar_init(&a_empty[i], 4);             // the four warps of the buffer's group
     }
     b200::mbar_init(xs_bar, 1);
     b200::mbar_init(done_bar, TC_ISSUERS);
@@ -880,28 +921,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------- producer ----------------
     // Weight tiles do not depend on the activation kernel (this grid's programmatic primary),
     // so the first ring of weight tiles is issued before griddepcontrol.wait; each stage's
-    // activation tiles (and the scales) only after it.
+    // activation tile (and the scales) only after it.
     if (lane == 0) {
       const uint64_t pol = b200::l2_policy_evict_first();
       const uint64_t wmap_addr = reinterpret_cast<uint64_t>(&wmap);
       auto issue_w = [&](int it) {
         const int s = it % nstage;
-        int blk, j;
-        wk.unit(it, blk, j);
+        int pr, kb;
+        wk.unit(it, pr, kb);
         b200::mbar_arrive_expect_tx(&w_full[s], STAGE);
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
             " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(b200::smem_u32(ring + s * STAGE)),
-            "l"(wmap_addr), "r"(0), "r"(0), "r"(blk * 8), "r"(j * KW), "r"(b200::smem_u32(&w_full[s])),
+            "l"(wmap_addr), "r"(0), "r"(0), "r"(pr * 16), "r"(kb), "r"(b200::smem_u32(&w_full[s])),
             "l"(pol)
             : "memory");
       };
       auto issue_x = [&](int it) {
         const int s = it % nstage;
-        int blk, j;
-        wk.unit(it, blk, j);
-        b200::bulk_g2s(ring + s * STAGE + KW * TC_TILE_W, qt + (long long)j * KW * XT_BYTES,
-                       KW * XT_BYTES, &w_full[s]);
+        int pr, kb;
+        wk.unit(it, pr, kb);
+        b200::bulk_g2s(ring + s * STAGE + TC_PAIR_W, qt + (long long)kb * XT_BYTES, XT_BYTES, &w_full[s]);
       };
       const int first = min(nstage, total);
       for (int it = 0; it < first; ++it) issue_w(it);
@@ -928,34 +968,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else if (warp <= TC_ISSUERS) {
-    // ---------------- MMA issuers: 128-K block number kbit goes to issuer kbit % TC_ISSUERS ----
+    // ---------------- MMA issuers: issuer `me` computes block 2p + me of every stage --------
     if (lane == 0) {
       const int me = warp - 1;
       const uint32_t idesc = (1u << 4)                        // D: f32
                              | ((uint32_t)(TPAD >> 3) << 17)  // N
                              | ((uint32_t)(128 >> 4) << 24);  // M = 128; A, B e4m3, K-major
       bool ok = true;
-      for (int it = 0; it < total && ok; ++it) {
+      for (int it = 0; it < total; ++it) {
         const int s = it % nstage;
-        if (KW < TC_ISSUERS && (it * KW) % TC_ISSUERS != me) continue;     // not my stage
         if (!b200::mbar_wait_bounded(&w_full[s], (it / nstage) & 1, deadline)) { ok = false; break; }
-        const uint32_t st = b200::smem_u32(ring + s * STAGE);
-        for (int q = 0; q < KW; ++q) {
-          const int kbit = it * KW + q;
-          if (kbit % TC_ISSUERS != me) continue;
-          const int buf = kbit % nbuf;
-          if (kbit >= nbuf && !b200::mbar_wait_bounded(&a_empty[buf], ((kbit / nbuf) - 1) & 1, deadline)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = sw128_desc(st + q * TC_TILE_W);
-          const uint64_t bd = sw128_desc(st + KW * TC_TILE_W + q * XT_BYTES);
-          const uint32_t d = tmem + (uint32_t)(buf * TPAD);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma_f8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
-          tc_commit(&a_full[buf]);
+        const int kk = 2 * it + me, buf = kk % nbuf;
+        if (kk >= nbuf && !b200::mbar_wait_bounded(&a_empty[buf], ((kk / nbuf) - 1) & 1, deadline)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t st = b200::smem_u32(ring + s * STAGE);
+        const uint64_t ad = sw128_desc(st + me * TC_TILE_W), bd = sw128_desc(st + TC_PAIR_W);
+        const uint32_t d = tmem + (uint32_t)(buf * TPAD);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc_mma_f8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
+        tc_commit(&a_full[buf]);
         tc_commit(&w_empty[s]);
       }
       if (!ok) atomicExch(&g_lmhead_err, 1);
@@ -964,105 +998,122 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue: group g handles block 2p + g of each pair ----------------
     // After a timed-out wait the warps carry on without touching TMEM (so every warp still
     // reaches the final barrier) and the error word reports the call.
+    const int ew = warp - 1 - TC_ISSUERS;     // 0..7
+    const int g = ew >> 2;
     const int qd = warp & 3;                  // TMEM lane quarter this warp may access
-    const int ew = warp - 1 - TC_ISSUERS;
     const int row = 32 * qd + lane;           // row of the 128-row block held by this lane
-    b200::RowStat st[TPAD / 32];
+    float* tr = reinterpret_cast<float*>(sm + p.x_off) + ew * (TC_CHUNK * 33);
 #pragma unroll
-    for (int i = 0; i < TPAD / 32; ++i) b200::rowstat_init(st[i]);
+    for (int i = 0; i < TPAD / TC_CHUNK; ++i) b200::rowstat_init(st[i]);
     bool ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xs_bar, 0, deadline));
-    int kbit = 0;
     for (int it = 0; it < total;) {
-      int blk, j0;
-      wk.unit(it, blk, j0);
+      int pr, j0;
+      wk.unit(it, pr, j0);
+      const int blk = 2 * pr + g;
+      const bool real = blk < nblk;
       float acc[TPAD];
 #pragma unroll
       for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
-      const float* wsrow = static_cast<const float*>(p.wscale) + (long long)blk * KB;
-      const float wsv = (lane < KB) ? __ldg(wsrow + lane) : 0.f;
+      const float* wsrow = static_cast<const float*>(p.wscale) + (long long)(real ? blk : 0) * KB;
+      const float wsv = (lane < KB && real) ? __ldg(wsrow + lane) : 0.f;
       int j1 = j0;
       for (;; ++it) {
-        int b2, jj;
+        int p2, kb;
         if (it >= total) break;
-        wk.unit(it, b2, jj);
-        if (b2 != blk) break;
-        j1 = jj;
-        for (int q = 0; q < KW; ++q, ++kbit) {
-          const int kb = jj * KW + q, buf = kbit % nbuf;
-          const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb & 31) : __ldg(wsrow + kb);
-          if (ok) ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (kbit / nbuf) & 1, deadline));
-          if (!ok) continue;
-          tc_fence_after();
-          const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
-          float v[TPAD];
-          tmem_ld_row<TPAD>(ta, v);
+        wk.unit(it, p2, kb);
+        if (p2 != pr) break;
+        j1 = kb;
+        const int kk = 2 * it + g, buf = kk % nbuf;
+        const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb & 31) : (real ? __ldg(wsrow + kb) : 0.f);
+        if (ok) ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (kk / nbuf) & 1, deadline));
+        if (!ok) continue;
+        tc_fence_after();
+        const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
+        const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
+#pragma unroll
+        for (int h = 0; h < TPAD / 32; ++h) {
+          float v[32];
+          tmem_ld32(ta + 32 * h, v);
           tmem_wait_ld();
           tmem_values_after_wait(v);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
-          const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
 #pragma unroll
-          for (int j = 0; j < TPAD; j += 4) {
-            const float4 xv = xs4[j >> 2];
-            acc[j] = fmaf(v[j], sw * xv.x, acc[j]);
-            acc[j + 1] = fmaf(v[j + 1], sw * xv.y, acc[j + 1]);
-            acc[j + 2] = fmaf(v[j + 2], sw * xv.z, acc[j + 2]);
-            acc[j + 3] = fmaf(v[j + 3], sw * xv.w, acc[j + 3]);
+          for (int j = 0; j < 32; j += 4) {
+            const float4 xv = xs4[(32 * h + j) >> 2];
+            acc[32 * h + j] = fmaf(v[j], sw * xv.x, acc[32 * h + j]);
+            acc[32 * h + j + 1] = fmaf(v[j + 1], sw * xv.y, acc[32 * h + j + 1]);
+            acc[32 * h + j + 2] = fmaf(v[j + 2], sw * xv.z, acc[32 * h + j + 2]);
+            acc[32 * h + j + 3] = fmaf(v[j + 3], sw * xv.w, acc[32 * h + j + 3]);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
       }
       if (j0 != 0 || j1 != wk.KBS - 1) {
-        // A block shared with other CTAs: publish this CTA's fp32 partial; tc_finish_kernel
-        // sums the partials in CTA order and writes the block.
-        float4* dst = reinterpret_cast<float4*>(p.px + ((long long)wk.slot(wk.c, blk) * 128 + row) * TPAD);
+        // A pair shared with other CTAs: publish this CTA's fp32 partial of block 2p + g as
+        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes); tc_finish_kernel sums
+        // the partials in CTA order and writes the block.
+        float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.slot(wk.c, pr) * 2 + g) * (TPAD / 4) * 128 + row;
 #pragma unroll
-        for (int j = 0; j < TPAD; j += 4) dst[j >> 2] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
         continue;
       }
-      tc_block_out<TPAD, STATS>(p, acc, blk, qd, lane, reinterpret_cast<float*>(sm + p.x_off) + ew * (32 * 33), st);
+      if (real) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, st);
     }
     if (!ok) atomicExch(&g_lmhead_err, 1);
-    if (STATS) {
-#pragma unroll
-      for (int i = 0; i < TPAD / 32; ++i) red[ew * 64 + 32 * i + lane] = st[i];
-    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();                          // every copy has landed and every MMA completed
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
   }
-  if (STATS) stats_write_partial(p, red, 64, 4, blockIdx.x, 2 * gridDim.x);
+  if (STATS) {
+    // the ring is idle now: the per-warp row statistics go there
+    b200::RowStat* red = reinterpret_cast<b200::RowStat*>(ring);
+    if (warp > TC_ISSUERS) {
+      const int ew = warp - 1 - TC_ISSUERS;
+      for (int i = 0; i < 64; i += 32) red[ew * 64 + i + lane] = b200::RowStat{-INFINITY, 0x7fffffff, 0.f};
+      __syncwarp();
+      if (lane < TC_CHUNK) {
+#pragma unroll
+        for (int i = 0; i < TPAD / TC_CHUNK; ++i) red[ew * 64 + TC_CHUNK * i + lane] = st[i];
+      }
+    }
+    __syncthreads();
+    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, 2 * gridDim.x);
+  }
 }
 
-// Completes the 128-row blocks fp8_tc_kernel split between CTAs: sums their fp32 partials in
-// CTA order, writes the block like the main kernel and puts its row statistics in partial
-// slot G + blockIdx.x (next to the main grid's G slots). Launched as the programmatic
-// dependent of fp8_tc_kernel with the same grid size G; 128 threads, thread = block row.
+// Completes the block pairs fp8_tc_kernel split between CTAs: sums their fp32 partials in CTA
+// order, writes both blocks like the main kernel and puts the row statistics in partial slot
+// G + blockIdx.x (next to the main grid's G slots). Launched as the programmatic dependent of
+// fp8_tc_kernel with the same grid size G; 256 threads: warp w handles rows 32 (w & 3) .. + 31
+// of block 2p + (w >> 2).
 template <int TPAD, bool STATS>
-__global__ void __launch_bounds__(128) tc_finish_kernel(Params p, int KBS) {
-  __shared__ float tr_all[4][32 * 33];
-  __shared__ b200::RowStat red[4 * 64];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = threadIdx.x;
+__global__ void __launch_bounds__(256) tc_finish_kernel(Params p, int KBS) {
+  __shared__ b200::RowStat red[8 * 64];
+  __shared__ float tr_all[8][TC_CHUNK * 33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = warp >> 2, qd = warp & 3, row = 32 * qd + lane;
   const int G = gridDim.x, nblk = p.N / 128;
-  const TcWork wk = tc_work(nblk, KBS, G, 0);
-  b200::RowStat st[TPAD / 32];
+  const TcWork wk = tc_work((nblk + 1) / 2, KBS, G, 0);
+  b200::RowStat st[TPAD / TC_CHUNK];
 #pragma unroll
-  for (int i = 0; i < TPAD / 32; ++i) b200::rowstat_init(st[i]);
+  for (int i = 0; i < TPAD / TC_CHUNK; ++i) b200::rowstat_init(st[i]);
   griddep_launch_dependents();              // stats_merge_kernel may be scheduled
   griddep_wait();                           // the main grid has finished; its writes are visible
-  // CTA c finishes the block in which main-grid CTA c's units start, when that start is inside
-  // a block whose first unit belongs to CTA c - 1: every split block has exactly one such c.
+  // CTA c finishes the pair in which main-grid CTA c's units start, when that start is inside
+  // a pair whose first unit belongs to CTA c - 1: every split pair has exactly one such c.
   const int c = blockIdx.x;
   const long long lu_c = wk.LU * c / G;
   if (c > 0 && lu_c % KBS != 0 && wk.owner(lu_c / KBS * KBS) == c - 1) {
-    const int b = (int)(lu_c / KBS);
-    const long long u0 = (long long)b * KBS;
+    const int pr = (int)(lu_c / KBS);
+    const int blk = 2 * pr + g;
+    const long long u0 = (long long)pr * KBS;
     float acc[TPAD];
 #pragma unroll
     for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
@@ -1071,10 +1122,10 @@ __global__ void __launch_bounds__(128) tc_finish_kernel(Params p, int KBS) {
       const int cc = wk.owner(u0 + u);
       if (cc == prev) continue;
       prev = cc;
-      const float4* src = reinterpret_cast<const float4*>(p.px + ((long long)wk.slot(cc, b) * 128 + row) * TPAD);
+      const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(cc, pr) * 2 + g) * (TPAD / 4) * 128 + row;
       float4 v4[TPAD / 4];
 #pragma unroll
-      for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j);
+      for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
 #pragma unroll
       for (int j = 0; j < TPAD / 4; ++j) {
         acc[4 * j] += v4[j].x;
@@ -1083,13 +1134,17 @@ __global__ void __launch_bounds__(128) tc_finish_kernel(Params p, int KBS) {
         acc[4 * j + 3] += v4[j].w;
       }
     }
-    tc_block_out<TPAD, STATS>(p, acc, b, warp, lane, tr_all[warp], st);
+    if (blk < nblk) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr_all[warp], st);
   }
   if constexpr (STATS) {
+    for (int i = 0; i < 64; i += 32) red[warp * 64 + i + lane] = b200::RowStat{-INFINITY, 0x7fffffff, 0.f};
+    __syncwarp();
+    if (lane < TC_CHUNK) {
 #pragma unroll
-    for (int i = 0; i < TPAD / 32; ++i) red[warp * 64 + 32 * i + lane] = st[i];
+      for (int i = 0; i < TPAD / TC_CHUNK; ++i) red[warp * 64 + TC_CHUNK * i + lane] = st[i];
+    }
     __syncthreads();
-    stats_write_partial(p, red, 64, 4, G + blockIdx.x, 2 * G);
+    stats_write_partial(p, red, 64, 8, G + blockIdx.x, 2 * G);
   }
 }
 
@@ -1139,7 +1194,7 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) 
   float sum = 0.f;
 #pragma unroll
   for (int k = 0; k < 2; ++k)
-    if (ps[k] > 0.f) sum += ps[k] * expf(pm[k] - mx);
+    if (ps[k] > 0.f) sum += ps[k] * __expf(pm[k] - mx);
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) {
@@ -1254,44 +1309,41 @@ int launch_m(const Params& p, cudaStream_t stream) {
 // Workspace: [0,16) ticket counter | [16, 16+1024*64*12) per-CTA row statistics |
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
 // [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
-// [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 blocks split between CTAs, two
-// [128][64] slots per CTA.
+// [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 block pairs split between CTAs:
+// two pairs per CTA, each two [128][64] blocks.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
 constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
 constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
-constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 2LL * TC_MAX_GRID * 128 * 64 * 4;
+constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 4LL * TC_MAX_GRID * 128 * 64 * 4;
 constexpr long long WORKSPACE_BYTES = PX_OFF + PX_CAP;
 static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
 
-// Shared-memory plan of the tcgen05 kernel: the widest stage (KW 128-K blocks, KW | K/128)
-// that still leaves at least 3 stages in the ring. Returns the dynamic smem bytes or -1.
+// Shared-memory plan of the tcgen05 kernel: header, row statistics, activation scales, then
+// as many pair stages (two weight tiles + one activation tile) as fit. Returns the dynamic
+// smem bytes or -1.
 int plan_tc(Params& p, int tpad) {
   const int KB = p.K / 128;
-  p.xs_off = TC_HDR + TC_RED;
-  p.x_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;          // 4 warps x [32][33] fp32 tiles
-  p.ring_off = (p.x_off + 4 * 32 * 33 * 4 + 1023) & ~1023;
+  p.xs_off = TC_HDR;
+  p.x_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;          // 8 warps x [16][33] fp32 tiles
+  p.ring_off = (p.x_off + TC_EPI_WARPS * TC_CHUNK * 33 * 4 + 1023) & ~1023;
   const int avail = SMEM_CAP - 1024 - p.ring_off;
-  for (int kw = 4; kw >= 1; kw >>= 1) {
-    if (KB % kw) continue;
-    const int stage = kw * (TC_TILE_W + tpad * 128);
-    const int nstage = min(TC_MAX_STAGES, avail / stage);
-    if (nstage >= 3 || (kw == 1 && nstage >= 2)) {
-      p.kw = kw;
-      p.nstage = nstage;
-      p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
-      return 1024 + p.ring_off + nstage * stage;
-    }
-  }
-  return -1;
+  const int stage = TC_PAIR_W + tpad * 128;
+  const int nstage = min(TC_MAX_STAGES, avail / stage);
+  if (nstage < 2) return -1;
+  p.kw = 1;
+  p.nstage = nstage;
+  p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
+  return 1024 + p.ring_off + nstage * stage;
 }
 
 // 4-D view of the strip-packed weight for the tensor-map copy: (byte 128, row 16, strip, kb),
-// the strip and kb strides swapped against memory order so that one (128, 16, 8, kw) box is
-// kw consecutive 128x128 tiles of one 128-row block, each landing as [128 rows][128 B] already
-// in the 128-byte-swizzled order (the pack stores it that way; the copy itself does not swizzle).
-int make_strip_map(CUtensorMap* m, const void* w, int N, int K, int kw) {
+// the strip and kb strides swapped against memory order so that one (128, 16, 16, 1) box is the
+// 128x128 tiles of two consecutive 128-row blocks at one 128-K block, each landing as
+// [128 rows][128 B] already in the 128-byte-swizzled order (the pack stores it that way; the
+// copy itself does not swizzle). Strips beyond N read as zeros.
+int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -1304,7 +1356,7 @@ int make_strip_map(CUtensorMap* m, const void* w, int N, int K, int kw) {
   const int KB = K / 128;
   cuuint64_t dims[4] = {128, 16, (cuuint64_t)(N / 16), (cuuint64_t)KB};
   cuuint64_t strides[3] = {128, (cuuint64_t)KB * 2048, 2048};
-  cuuint32_t box[4] = {128, 16, 8, (cuuint32_t)kw};
+  cuuint32_t box[4] = {128, 16, 16, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(w), dims, strides, box,
                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1321,7 +1373,7 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   const int smem = plan_tc(p, TPAD);
   if (smem < 0) return -8;
   CUtensorMap wmap;
-  if (make_strip_map(&wmap, p.w, p.N, p.K, p.kw) != 0) return -12;
+  if (make_strip_map(&wmap, p.w, p.N, p.K) != 0) return -12;
   char* base = reinterpret_cast<char*>(p.counter);
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
@@ -1334,11 +1386,12 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   p.pdl = 1;
-  const long long units = (long long)(p.N / 128) * (KB / p.kw);
+  const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
   const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
+  if (units * grid >= (1LL << 31)) return -8;               // the kernels' work arithmetic is 32-bit
   rc = launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
   if (rc != 0) return rc;
-  rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(128), 0, stream, true, p, KB / p.kw);
+  rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(256), 0, stream, true, p, KB);
   if (rc != 0 || !STATS) return rc;
   return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, 2 * grid);
 }
@@ -1552,7 +1605,7 @@ int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
 // b200_fp8_lmhead needs a caller-owned workspace. Some callers cannot hand one over: a plain C
 // or ctypes binding that has no device allocator of its own, or code running where an
 // allocation is not allowed (a caching allocator's hook, a memory-capped pool). For those the
-// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 12.3 MB per
+// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 22.3 MB per
 // device, reserved when the library's device code is loaded).
 
 namespace {
