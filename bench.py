@@ -1,18 +1,18 @@
 """Benchmark of the B200 decode hot path (one JSON line on rank 0).
 
-Headline workload (the config timed at 1/2/4/8 GPUs): the FP8 target
-lm_head, N=151936 x K=2560, M=64 token rows, vocab-sharded on 128-row blocks across the
-ranks; one step = the fused per-token-group quant + block-scaled GEMV + (max, argmax,
-logsumexp) epilogue on this rank's shard, then the all-gather combine of those triples.
-``value`` = algorithmic bytes of the whole head (weights + block scales + activation +
-logits + stats, the formula of BASELINE.md) / max-over-ranks step time, aggregated over all
-ranks (strong scaling: total work fixed). Weights are rotated through a pool larger than
-2.5x the 126 MB L2 so every step streams from HBM.
+Headline workload (the configuration timed at 1/2/4/8 GPUs): the FP8 target lm_head,
+N=151936 x K=2560, M=64 token rows, vocab-sharded on 128-row blocks across the ranks; one
+step = the fused per-token-group quant + block-scaled tcgen05 GEMM + (max, argmax, logsumexp)
+epilogue on this rank's shard, then the all-gather combine of those triples. ``value`` =
+algorithmic bytes of the whole head (weights N*K + block scales + bf16 activation + bf16
+logits + 12 B of statistics per token) / max-over-ranks step time, aggregated over all ranks
+(strong scaling: total work fixed). Weights are rotated through a pool larger than 2.5x the
+126 MB L2 so every step streams from HBM.
 
 Secondary numbers in the same line: the expert-id-sharded LRU cache update (52 layers, the
 fused manage+align kernel, Zipf(1.1) routing) in us/layer; and on rank 0 at N=1 the other
-BASELINE configs -- FP8 head at M in {1,5,20}, W4 draft head at M=4, SiLU-quant [8, 2x512] --
-each as us/call and GB/s. ``cpu_baseline`` times the oracle's torch-CPU restatement of the
+configurations of the path -- FP8 head at M in {1,5,20}, W4 draft head at M=4, SiLU-quant
+[8, 2x512] -- each as us/call and GB/s. ``cpu_baseline`` times the oracle's torch-CPU restatement of the
 FP8 head on a bounded vocabulary sample.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
@@ -43,7 +43,8 @@ E_EXPERTS, S_SLOTS, LAYERS, TOPK = 512, 257, 52, 10
 
 
 def fp8_bytes(n_rows: int, k: int, m: int) -> int:
-    """Algorithmic bytes of one FP8 head call (BASELINE.md formula)."""
+    """Algorithmic bytes of one FP8 head call: weights + block scales + bf16 activation +
+    bf16 logits + 12 B of (max, argmax, logsumexp) per token."""
     return n_rows * k + (n_rows // 128) * (k // 128) * 4 + m * k * 2 + m * n_rows * 2 + m * 12
 
 
@@ -239,7 +240,7 @@ def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
 
 
 def ops_bench(P, dev) -> dict:
-    """The other BASELINE configs on one GPU: us/call in a CUDA graph over a pool > L2."""
+    """The secondary configurations on one GPU: us/call in a CUDA graph over a pool > L2."""
     pk = peaks()["hbm_gbs"]
     res = {}
     pool = make_fp8_pool(P, N_VOCAB, dev, 0)
@@ -388,7 +389,8 @@ def main():
     torch.manual_seed(0)
     x = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
     y = torch.empty(M_ROWS, n_loc, dtype=torch.bfloat16, device=dev)
-    launches_per_step = 2 * math.ceil(M_ROWS / 64)      # activation tiles + tcgen05 GEMM
+    # per 64-token chunk: activation tiles, tcgen05 GEMM, split-block finish, statistics merge
+    launches_per_step = 4 * math.ceil(M_ROWS / 64)
 
     def step(i, kev=None):
         wq, ws = pool[i % len(pool)]
@@ -501,7 +503,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                          "peak_source": pk["source"], "kernel_us": kern_us_max,
-                         "kernel": "act_tiles_kernel + fp8_tc_kernel<64> (tcgen05)",
+                         "kernel": "fp8_tc_kernel<64> (tcgen05); timed with its launch set "
+                                   "(act_tiles + tc + finish + merge), so achieved is a lower bound",
                          "bytes_per_launch_set": per_launch_bytes,
                          "read_control_GB_s": ceiling},
             "cpu_baseline": cpu,

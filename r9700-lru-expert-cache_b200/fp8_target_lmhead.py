@@ -12,7 +12,7 @@ it as 16-row strips, ``[N/16][K/128][16 rows][128 B]`` with the 16-byte chunk c 
 chunk ``c ^ (r & 7)`` -- one bulk copy per strip run for the GEMV, and the 128-byte-swizzled
 K-major tile a tensor-core operand expects. ``unpack_fp8_block`` restores row-major order.
 
-``fp8_lmhead`` is the fused entry BASELINE asks for: logits plus per-row max, argmax and
+``fp8_lmhead`` is the fused entry: logits plus per-row max, argmax and
 logsumexp in the same pass over the weight.
 """
 from __future__ import annotations

@@ -7,7 +7,7 @@ statistics (max within 1e-3 relative, logsumexp within 1e-3 absolute, argmax exa
 the oracle's top-2 gap is below 1e-3); max |dlogit| and |dlogprob| printed. W4: against
 ``F.linear(x.half().float(), unpack_w4(p))`` with the reference's rel-Frobenius < 5e-3
 (tests/k3/w4_verify.py:35-56) over M in {1,2,3,5,16,20,64,129} and N=1000 padding.
-Both at the BASELINE shape N=151936, K=2560 too. Graph replay == eager."""
+Both at the full head shape N=151936, K=2560 too. Graph replay == eager."""
 from __future__ import annotations
 
 import pytest
@@ -80,7 +80,7 @@ def test_fp8_prequantized_abi(cuda):
 
 @pytest.mark.parametrize("M", [1, 5, 20])
 def test_fp8_fused_baseline_shape(cuda, M):
-    """W ~N(0,0.02) [151936, 2560], x ~N(0,1)."""
+    """Full target head: W ~N(0,0.02) [151936, 2560], x ~N(0,1)."""
     N, K = 151936, 2560
     wq, ws, wdq = _fp8_weight(N, K, 0, cuda)
     x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16, generator=torch.Generator(device=cuda).manual_seed(M))
@@ -199,7 +199,7 @@ def test_w4_reference_c_abi_f16(cuda):
 
 
 def test_w4_baseline_shape(cuda):
-    """x [4, 2560] ~N(0,1), W ~N(0,0.02) [151936, 2560]."""
+    """Full draft head: x [4, 2560] ~N(0,1), W ~N(0,0.02) [151936, 2560]."""
     n, k, M = 151936, 2560, 4
     w = (torch.randn(n, k, device=cuda, generator=torch.Generator(device=cuda).manual_seed(0)) * 0.02).bfloat16()
     p = W4.pack_w4a16(w)

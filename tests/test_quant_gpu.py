@@ -2,7 +2,7 @@
 
 Bit-exact (activation, scales, FP8 bytes) against the torch-GPU eager restatement in
 oracle/quant_oracle.py over the reference probe's grid (tests/k4/probe_silu_quant.py:22-53:
-rows {1,10,50,80,2048} x d {320,640} x input scale {1, 1e-3, 60}) plus BASELINE's
+rows {1,10,50,80,2048} x d {320,640} x input scale {1, 1e-3, 60}) plus the decode
 [8, 2x512] bf16 case, f16 inputs, strided and unaligned rows, the zero row; and against
 vLLM's silu_and_mul + scaled_fp8_quant pair when those ops load here. The CPU oracle is
 compared too and the number of CPU/GPU expf disagreements is reported."""
@@ -41,7 +41,7 @@ def test_silu_quant_bit_exact_grid(cuda, rows, d, sc):
 
 
 def test_silu_quant_baseline_config_and_cpu_oracle(cuda):
-    """BASELINE config: bf16 [8, 2x512] ~N(0,1) from seed 0. GPU exact; CPU oracle compared
+    """Decode config: bf16 [8, 2x512] ~N(0,1) from seed 0. GPU exact; CPU oracle compared
     and its (expf-ulp) disagreements reported."""
     torch.manual_seed(0)
     x = torch.randn(8, 1024, dtype=torch.bfloat16)
