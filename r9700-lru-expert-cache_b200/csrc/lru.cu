@@ -52,11 +52,13 @@ constexpr long long KEY_MAX = 0x7fffffffffffffffLL;
 constexpr unsigned KEY32_MAX = 0xffffffffu;
 constexpr int AGE_BITS = 21;              // 32-bit keys: (2^21 - 1 - age) << 11 | slot
 constexpr int IDS_REG = 4;                // topk ids kept in registers: mk <= IDS_REG * NT
+constexpr int SEL_MAX = 32;               // warp-selection victim path: nins <= SEL_MAX
+constexpr int SMALL_MK = 128;             // direct-ranking align path: mk <= SMALL_MK
 
 // Shared-memory carve-up (bytes), all offsets 16-byte aligned.
 struct Smem {
-  int off_red, off_flags, off_tab, off_se, off_st, off_k64, off_k32, off_vic, off_missE;
-  int off_cnt_h, off_cum_h, off_cnt_c, off_cum_c, total;
+  int off_red, off_flags, off_tab, off_se, off_st, off_k64, off_k32, off_vic, off_missE, off_cand;
+  int off_cnt_h, off_cum_h, off_cnt_c, off_cum_c, off_key, off_tc, total;
 };
 
 __host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
@@ -74,13 +76,16 @@ __host__ __device__ inline Smem smem_layout(int E, int S, bool tab_smem, bool fu
   L.off_k32 = o;   o += align16(S4 * 4);
   L.off_vic = o;   o += align16(MAXINS * 4);
   L.off_missE = o; o += align16(MAXINS * 4);
+  L.off_cand = o;  o += align16(NW * SEL_MAX * 4);
   if (fused) {
     L.off_cnt_h = o; o += align16(S * 4);
     L.off_cum_h = o; o += align16(S * 4);
     L.off_cnt_c = o; o += align16(E * 4);
     L.off_cum_c = o; o += align16(E * 4);
+    L.off_key = o;   o += align16(SMALL_MK * 4);
+    L.off_tc = o;    o += align16(SMALL_MK * 4);
   } else {
-    L.off_cnt_h = L.off_cum_h = L.off_cnt_c = L.off_cum_c = 0;
+    L.off_cnt_h = L.off_cum_h = L.off_cnt_c = L.off_cum_c = L.off_key = L.off_tc = 0;
   }
   L.total = o;
   return L;
@@ -99,14 +104,11 @@ __device__ __forceinline__ void block_sum_exscan(int a, int b, int* ra, int* rb,
     rb[w] = inc;
   }
   __syncthreads();
-  int sa = 0, before = 0, tb = 0;
-#pragma unroll
-  for (int i = 0; i < NW; ++i) {
-    sa += ra[i];
-    const int x = rb[i];
-    before += (i < w) ? x : 0;
-    tb += x;
-  }
+  // lane i < NW of every warp picks up warp i's totals; shuffles combine them
+  const int xa = (l < NW) ? ra[l] : 0, xb = (l < NW) ? rb[l] : 0;
+  const int sa = __reduce_add_sync(0xffffffffu, xa);
+  const int tb = __reduce_add_sync(0xffffffffu, xb);
+  const int before = __reduce_add_sync(0xffffffffu, (l < w) ? xb : 0);
   *sum_a = sa;
   *pre_b = before + inc - b;
   *tot_b = tb;
@@ -250,8 +252,41 @@ __device__ void manage_core(const ManageArgs& a, char* sm, const Smem& L, int (&
   block_sum_exscan(nev, nofit, red + 2 * NW, red + 3 * NW, &nev_total, &dummy, &nofit_total);  // B4
   const int nact = min(nins, nev_total);
 
-  // ---- 5. rank each evictable key against all keys: rank r < nins -> victim r -------------
-  if (nofit_total == 0) {
+  // ---- 5. victims: the nins smallest keys, victim r = the slot of the r-th smallest --------
+  // Keys are unique (the slot is in the low bits), so ranks are well defined. Few inserts
+  // (nins <= 32, 32-bit keys, S <= 1024): each warp takes its 64 keys and pulls out its own
+  // nins smallest with warp min-reductions; the block's nins smallest are among those
+  // candidates, so ranking the candidates against one another names the victims.
+  if (nofit_total == 0 && nins <= SEL_MAX) {
+    unsigned* cand = reinterpret_cast<unsigned*>(sm + L.off_cand);
+    const int w = tid >> 5, l = tid & 31;
+    const int i0 = 32 * w + l, i1 = 32 * (w + NW) + l;
+    const unsigned ka = (i0 < S) ? s_k32[i0] : KEY32_MAX;
+    const unsigned kb = (i1 < S) ? s_k32[i1] : KEY32_MAX;
+    unsigned lo2 = min(ka, kb), hi2 = max(ka, kb);
+    for (int r = 0; r < nins; ++r) {
+      const unsigned m = __reduce_min_sync(0xffffffffu, lo2);
+      if (l == 0) cand[w * nins + r] = m;
+      if (lo2 == m) {                       // the (unique) owner moves to its next key
+        lo2 = hi2;
+        hi2 = KEY32_MAX;
+      }
+    }
+    __syncthreads();
+    const int nc = NW * nins;               // a multiple of 16, so uint4 reads cover it
+    for (int c = tid; c < nc; c += NT) {
+      const unsigned k = cand[c];
+      if (k == KEY32_MAX) continue;
+      const uint4* cv = reinterpret_cast<const uint4*>(cand);
+      int r = 0;
+#pragma unroll 8
+      for (int j = 0; j < (nc >> 2); ++j) {
+        const uint4 q = cv[j];
+        r += (q.x < k) + (q.y < k) + (q.z < k) + (q.w < k);
+      }
+      if (r < nins) s_vic[r] = (int)(k & 0x7ffu);
+    }
+  } else if (nofit_total == 0) {
     const unsigned k0 = (tid < S) ? s_k32[tid] : KEY32_MAX;
     const unsigned k1 = (tid + NT < S) ? s_k32[tid + NT] : KEY32_MAX;
     if (k0 != KEY32_MAX || k1 != KEY32_MAX) {
@@ -385,6 +420,73 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
     const int s = s_tab[e];
     return ((unsigned)s < (unsigned)S) ? s : (MAXS + e);
   };
+  auto padded = [&](int c) { return (c + bs - 1) / bs * bs; };
+
+  if (mk <= SMALL_MK) {
+    // ---- few routed ids (decode): every token ranks itself directly --------------------------
+    // Token i's slot in its side's sorted list = (padded sizes of that side's buckets with a
+    // smaller key) + (tokens of its own bucket with a smaller index): the same stable order as
+    // the counting sort below, from two O(mk) passes per token and no bucket scans. Padding
+    // sentinels go in first, in parallel; the token writes come two barriers later.
+    int* s_key = reinterpret_cast<int*>(sm + L.off_key);
+    int* s_tc = reinterpret_cast<int*>(sm + L.off_tc);
+    for (int p = tid; p < f.L; p += NT) {
+      f.sorted_hot[p] = mk;
+      f.sorted_cold[p] = mk;
+    }
+    // keys padded to a multiple of 4 with -1 so the passes read int4 vectors
+    const int key = (tid < mk) ? bucket_of(ids[0]) : -1;
+    const int mk4 = (mk + 3) & ~3;
+    if (tid < mk4) s_key[tid] = key;
+    __syncthreads();
+    int cnt = 0, eqb = 0;
+    const int4* kv = reinterpret_cast<const int4*>(s_key);
+    if (key >= 0) {
+#pragma unroll 4
+      for (int j = 0; j < (mk4 >> 2); ++j) {
+        const int4 q = kv[j];
+        const int j0 = 4 * j;
+        const int a0 = q.x == key, a1 = q.y == key, a2 = q.z == key, a3 = q.w == key;
+        cnt += a0 + a1 + a2 + a3;
+        eqb += (j0 < tid ? a0 : 0) + (j0 + 1 < tid ? a1 : 0) + (j0 + 2 < tid ? a2 : 0) + (j0 + 3 < tid ? a3 : 0);
+      }
+    }
+    // s_tc[j]: the padded size of token j's bucket if j is the bucket's first token, else 0
+    if (tid < mk4) s_tc[tid] = (key >= 0 && eqb == 0) ? padded(cnt) : 0;
+    __syncthreads();
+    int ph = 0, pc = 0;
+    if (key >= 0) {
+      const bool hot = key < MAXS;
+      // same side and a smaller key: hot keys are < MAXS <= cold keys, so for a cold token
+      // the hot keys must be excluded explicitly
+      const int lo_key = hot ? 0 : MAXS;
+      const int4* pv = reinterpret_cast<const int4*>(s_tc);
+      int before = 0;
+#pragma unroll 4
+      for (int j = 0; j < (mk4 >> 2); ++j) {
+        const int4 q = kv[j], pq = pv[j];
+        before += ((q.x >= lo_key && q.x < key) ? pq.x : 0) + ((q.y >= lo_key && q.y < key) ? pq.y : 0) +
+                  ((q.z >= lo_key && q.z < key) ? pq.z : 0) + ((q.w >= lo_key && q.w < key) ? pq.w : 0);
+      }
+      const int pos = before + eqb;
+      if (pos < f.L) (hot ? f.sorted_hot : f.sorted_cold)[pos] = tid;
+      if (eqb == 0) {                       // first token of its bucket: the bucket's block ids
+        const int bkt = hot ? key : key - MAXS, pn = padded(cnt);
+        int* eids = hot ? f.eids_hot : f.eids_cold;
+        for (int blk = before / bs; blk < (before + pn) / bs && blk < f.NB; ++blk) eids[blk] = bkt;
+        (hot ? ph : pc) = pn;
+      }
+    }
+    int tot_h, tot_c, unused;
+    block_sum_exscan(ph, pc, red + 6 * NW, red + 7 * NW, &tot_h, &unused, &tot_c);
+    if (tid == 0) {
+      f.npad_hot[0] = tot_h;
+      f.npad_cold[0] = tot_c;
+    }
+    for (int blk = tot_h / bs + tid; blk < f.NB; blk += NT) f.eids_hot[blk] = -1;
+    for (int blk = tot_c / bs + tid; blk < f.NB; blk += NT) f.eids_cold[blk] = -1;
+    return;
+  }
 
   // ---- counts (shared atomics: the counts do not depend on the order) --------------------
 #pragma unroll
