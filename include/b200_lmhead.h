@@ -36,8 +36,9 @@ int b200_silu_mul_quant(const void* x, int rows, int d, long long stride_x, int 
 int b200_per_token_group_quant_fp8(const void* x, int M, int K, long long stride_x, int dtype,
                                    int group, void* q, float* s, cudaStream_t stream);
 
-/* Bytes of the zero-initialised scratch the fused lm_head entries use (per-CTA row
- * statistics and a ticket counter); each call leaves it zeroed again. */
+/* Bytes of the caller-owned scratch the fused lm_head entries use (activation tiles and rows,
+ * per-CTA row statistics, partial accumulators). It needs no initialisation; calls that share
+ * it must not overlap on the GPU. */
 long long b200_lmhead_workspace_bytes(void);
 
 /* Device error word (1 = a bounded pipeline wait timed out); reset != 0 clears it. Synchronous. */
@@ -46,13 +47,13 @@ int b200_lmhead_error(int reset);
 /* Fused FP8 target lm_head (replaces gemm_fp8_block = per_token_group_quant_fp8 +
  * fp8hip_block_scaled_mm, kernels/fp8_target_lmhead.py:70-74, and adds the row statistics).
  * x bf16 [M, K]; wq / ws packed as above over N rows (N % 128 == 0, K % 128 == 0); y bf16
- * [M, ldy] (nullable); row_max fp32 [M], row_arg int32 [M] = first argmax + vocab_offset,
+ * [M, ldy] (nullable); row_max fp32 [M], row_arg int64 [M] = first argmax + vocab_offset,
  * row_lse fp32 [M] (each nullable; any of them needs the workspace); qx_out e4m3 [M, K] and
  * xs_out fp32 [M, K/128] (nullable) receive the quantized activation.
  * Returns -1 M < 0, -2 N % 128, -3 K % 128, -8 shape exceeds shared memory, -9 workspace
  * missing / too small, -10 misaligned pointer. */
 int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
-                    long long vocab_offset, void* y, long long ldy, float* row_max, int* row_arg,
+                    long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
                     float* row_lse, void* qx_out, float* xs_out, void* workspace,
                     long long workspace_bytes, cudaStream_t stream);
 
@@ -63,7 +64,7 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
  * not overlap on the GPU. */
 int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
                                    int N, long long vocab_offset, void* y, long long ldy,
-                                   float* row_max, int* row_arg, float* row_lse, void* qx_out,
+                                   float* row_max, long long* row_arg, float* row_lse, void* qx_out,
                                    float* xs_out, cudaStream_t stream);
 
 /* The closed fp8hip GEMM's ABI (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K]
@@ -91,7 +92,7 @@ int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream)
  * b200_fp8_lmhead plus -11 bad dtype. */
 int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
                    int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
-                   float* row_max, int* row_arg, float* row_lse, void* workspace,
+                   float* row_max, long long* row_arg, float* row_lse, void* workspace,
                    long long workspace_bytes, cudaStream_t stream);
 
 /* r4d_gemm_w4a16_nt_m64 (ABI bound at kernels/draft_w4_lmhead.py:118-127): f16 a [M, K],

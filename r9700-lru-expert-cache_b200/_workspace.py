@@ -1,6 +1,6 @@
-"""Caller-owned scratch for the fused lm_head entries (per-CTA row statistics + a ticket
-counter). One zero-initialised buffer per (device, stream); each call leaves it zeroed
-again, so calls on one stream reuse it. Calls that share a buffer must not overlap."""
+"""Caller-owned scratch for the fused lm_head entries (activation tiles and rows, per-CTA row
+statistics, partial accumulators). One buffer per (device, stream), reused by every call on
+that stream; it needs no initialisation. Calls that share a buffer must not overlap."""
 from __future__ import annotations
 
 import torch
@@ -16,6 +16,6 @@ def workspace(device: torch.device) -> torch.Tensor:
     ws = _WS.get(key)
     if ws is None:
         nbytes = int(_lib.lmhead().b200_lmhead_workspace_bytes())
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
         _WS[key] = ws
     return ws

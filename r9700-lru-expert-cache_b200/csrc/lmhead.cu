@@ -69,11 +69,11 @@ struct Params {
   __nv_bfloat16* y;
   long long ldy;
   float* row_max;
-  int* row_arg;
+  long long* row_arg;
   float* row_lse;
   uint8_t* qx_out;
   float* xs_out;
-  unsigned* counter;
+  char* ws;          // workspace base (nullptr: none)
   float* partial;
   int kps;           // 128-K blocks per stage (tcgen05 path: TMEM accumulators)
   int nstage;
@@ -287,9 +287,9 @@ __device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32
   }
 }
 
-// ---- row statistics: CTA partial per token, then the last CTA to finish merges them ---------
+// ---- row statistics: CTA partial per token, merged by stats_merge_kernel ---------------------
 // red[w * stride + m] holds warp w's state for token m (nred warps). The workspace partials
-// are token-major ([m][slot], G slots) so the final merge reads them coalesced.
+// are token-major ([m][slot], G slots) so the merge reads them coalesced.
 
 // Write this CTA's merged state per token into partial slot `slot`. Every thread calls it
 // after a barrier that published `red`.
@@ -303,83 +303,6 @@ __device__ __forceinline__ void stats_write_partial(const Params& p, const b200:
     dst[0] = r.m;
     dst[1] = __int_as_float(r.idx);
     dst[2] = r.s;
-  }
-}
-
-// Merge all G partial slots per token into row_max / row_arg / row_lse (one CTA).
-__device__ void stats_merge_all(const Params& p, int G);
-
-// Partial into slot blockIdx.x of gridDim.x, then a ticket; the last CTA of the grid merges
-// and resets the ticket.
-__device__ void stats_finalize(const Params& p, const b200::RowStat* red, int stride, int nred,
-                               int* s_flag) {
-  const int G = gridDim.x;
-  stats_write_partial(p, red, stride, nred, blockIdx.x, G);
-  if (threadIdx.x < p.M) __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned ticket = atomicAdd(p.counter, 1u);
-    *s_flag = (ticket == (unsigned)G - 1) ? 1 : 0;
-  }
-  __syncthreads();
-  if (*s_flag == 0) return;
-  __threadfence();
-  stats_merge_all(p, G);
-  if (threadIdx.x == 0) *p.counter = 0u;    // ready for the next call on this workspace
-}
-
-__device__ void stats_merge_all(const Params& p, int G) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  // Two tokens per warp at a time, all of a lane's partials loaded before any merge, so the
-  // merge costs a few memory round trips instead of one per partial.
-  constexpr int PER = 5;                      // 160 CTAs per pass
-  for (int m0 = warp; m0 < p.M; m0 += 2 * nwarps) {
-    const int mm[2] = {m0, m0 + nwarps};
-    b200::RowStat r[2];
-    b200::rowstat_init(r[0]);
-    b200::rowstat_init(r[1]);
-    for (int cb = 0; cb < G; cb += 32 * PER) {
-      float a[2][PER][3];
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          const int c = cb + lane + 32 * i;
-          if (c < G && mm[t] < p.M) {
-            const float* src = p.partial + ((long long)mm[t] * G + c) * 3;
-            a[t][i][0] = __ldcg(src);
-            a[t][i][1] = __ldcg(src + 1);
-            a[t][i][2] = __ldcg(src + 2);
-          } else {
-            a[t][i][0] = -INFINITY;
-            a[t][i][1] = __int_as_float(0x7fffffff);
-            a[t][i][2] = 0.f;
-          }
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          b200::RowStat o;
-          o.m = a[t][i][0];
-          o.idx = __float_as_int(a[t][i][1]);
-          o.s = a[t][i][2];
-          r[t] = b200::rowstat_merge(r[t], o);
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-#pragma unroll
-      for (int msk = 1; msk < 32; msk <<= 1) r[t] = b200::rowstat_merge(r[t], b200::rowstat_shfl_xor(r[t], msk));
-      if (lane == 0 && mm[t] < p.M) {
-        const int m = mm[t];
-        if (p.row_max) p.row_max[m] = r[t].m;
-        if (p.row_arg) p.row_arg[m] = r[t].idx;
-        if (p.row_lse) p.row_lse[m] = r[t].m + logf(r[t].s);
-      }
-    }
   }
 }
 
@@ -408,7 +331,6 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* x_bar = reinterpret_cast<uint64_t*>(sm + GEMV_XBAR);
   b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + GEMV_HDR_RED);   // [NC][MAXM]
-  int* s_flag = reinterpret_cast<int*>(sm + GEMV_HDR_RED + NC * MAXM * sizeof(b200::RowStat));
   char* ring = sm + p.ring_off;
 
   if (threadIdx.x == 0) {
@@ -421,6 +343,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   }
   __syncthreads();
   const uint64_t deadline = b200::globaltimer_ns() + WAIT_NS;
+  if (STATS) griddep_launch_dependents();   // stats_merge_kernel may be scheduled
 
   b200::RowStat st[NT8][2];
 #pragma unroll
@@ -544,7 +467,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 
   if (!STATS) return;
   __syncthreads();
-  stats_finalize(p, red, MAXM, NC, s_flag);
+  stats_write_partial(p, red, MAXM, NC, blockIdx.x, gridDim.x);
 }
 
 // ---- tcgen05 path: 16 < M <= 64 tokens ---------------------------------------------------------
@@ -1298,7 +1221,9 @@ int launch_one(Params p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int grid = min(p.N / 16, num_sms());
-  return launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
+  const int rc = launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
+  if (rc != 0 || !STATS) return rc;
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, grid);
 }
 
 template <int KIND, bool STATS>
@@ -1306,7 +1231,7 @@ int launch_m(const Params& p, cudaStream_t stream) {
   return (p.M <= 8) ? launch_one<KIND, 1, STATS>(p, stream) : launch_one<KIND, 2, STATS>(p, stream);
 }
 
-// Workspace: [0,16) ticket counter | [16, 16+1024*64*12) per-CTA row statistics |
+// Workspace: [0,16) reserved | [16, 16+1024*64*12) per-CTA row statistics |
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
 // [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
 // [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 block pairs split between CTAs:
@@ -1374,7 +1299,7 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   if (smem < 0) return -8;
   CUtensorMap wmap;
   if (make_strip_map(&wmap, p.w, p.N, p.K) != 0) return -12;
-  char* base = reinterpret_cast<char*>(p.counter);
+  char* base = p.ws;
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
   p.px = reinterpret_cast<float*>(base + PX_OFF);
@@ -1410,7 +1335,7 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
   const int M = p.M, KB = p.K / 128;
   const bool stats = (p.row_max || p.row_arg || p.row_lse);
   const bool is_fp8 = (KIND == FP8_QUANT || KIND == FP8_PREQ);
-  const bool have_ws = p.counter != nullptr;
+  const bool have_ws = p.ws != nullptr;
   const bool tc_ok = is_fp8 && have_ws && (long long)KB * 64 * 128 <= QT_CAP;
   const int chunk = tc_ok ? 64 : MAXM;
   for (int m0 = 0; m0 < M; m0 += chunk) {
@@ -1430,7 +1355,7 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
       rc = stats ? launch_tc<true>(q, qx_in, q.xs_in, stream) : launch_tc<false>(q, qx_in, q.xs_in, stream);
     } else if (KIND == FP8_QUANT && have_ws && (long long)MAXM * p.K <= QR_CAP) {
       // quantize the rows once (the programmatic primary), then the GEMV on e4m3 rows
-      char* base = reinterpret_cast<char*>(p.counter);
+      char* base = p.ws;
       uint8_t* qr = q.qx_out ? q.qx_out : reinterpret_cast<uint8_t*>(base + QR_OFF);
       float* sr = q.xs_out ? q.xs_out : reinterpret_cast<float*>(base + SR_OFF);
       rc = launch_ex(act_rows_kernel, dim3(KB, (q.M + 7) / 8), dim3(128), 0, stream, false,
@@ -1456,8 +1381,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 extern "C" {
 
-// Bytes of caller-owned workspace the fused entries need (zero-initialised once; every call
-// leaves it zeroed again). Calls that share a workspace must not overlap on the GPU.
+// Bytes of caller-owned workspace the fused entries need. It needs no initialisation (every
+// call writes what it reads); calls that share a workspace must not overlap on the GPU.
 long long b200_lmhead_workspace_bytes(void) { return WORKSPACE_BYTES; }
 
 // Reads (and with reset != 0 clears) the device error word: 1 = a pipeline wait timed out.
@@ -1480,7 +1405,7 @@ int b200_lmhead_error(int reset) {
 // Returns 0, -1 bad M, -2 N % 128, -3 K % 128, -8 does not fit shared memory, -9 workspace
 // too small / missing when stats are asked for, -10 misaligned pointer, else a CUDA error.
 int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
-                    long long vocab_offset, void* y, long long ldy, float* row_max, int* row_arg,
+                    long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
                     float* row_lse, void* qx_out, float* xs_out, void* workspace,
                     long long workspace_bytes, cudaStream_t stream) {
   if (M < 0) return -1;
@@ -1496,7 +1421,7 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
   p.y = static_cast<__nv_bfloat16*>(y); p.ldy = ldy > 0 ? ldy : N;
   p.row_max = row_max; p.row_arg = row_arg; p.row_lse = row_lse;
   p.qx_out = static_cast<uint8_t*>(qx_out); p.xs_out = xs_out;
-  p.counter = static_cast<unsigned*>(workspace);
+  p.ws = static_cast<char*>(workspace);
   p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
   return run_chunks<FP8_QUANT>(p, 2, stream);
 }
@@ -1553,7 +1478,7 @@ int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream)
 // -10 alignment, -11 bad dtype.
 int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
                    int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
-                   float* row_max, int* row_arg, float* row_lse, void* workspace,
+                   float* row_max, long long* row_arg, float* row_lse, void* workspace,
                    long long workspace_bytes, cudaStream_t stream) {
   if (M < 0) return -1;
   if (N_pad <= 0 || N_pad % 16) return -2;
@@ -1570,7 +1495,7 @@ int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, con
   p.w = static_cast<const uint8_t*>(wq); p.wscale = wsz;
   p.y = static_cast<__nv_bfloat16*>(y); p.ldy = ldy > 0 ? ldy : N_pad;
   p.row_max = row_max; p.row_arg = row_arg; p.row_lse = row_lse;
-  p.counter = static_cast<unsigned*>(workspace);
+  p.ws = static_cast<char*>(workspace);
   p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
   return x_dtype == 0 ? run_chunks<W4_BF16>(p, 2, stream) : run_chunks<W4_F16>(p, 2, stream);
 }
@@ -1645,11 +1570,11 @@ extern "C" {
 // b200_fp8_lmhead with the library's own scratch instead of a workspace argument; same
 // operands, outputs and return codes, plus -9 K > STATIC_SCRATCH_MAX_K and -13 device index
 // >= 64. The first call on each device looks the scratch up (make it before capturing a
-// stream). Every call first clears the scratch's ticket counter on `stream`. One array serves
+// stream). The scratch needs no clearing: every call writes what it reads. One array serves
 // every stream of a device, so calls that overlap on the GPU race on it: run them in order.
 int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
                                    int N, long long vocab_offset, void* y, long long ldy,
-                                   float* row_max, int* row_arg, float* row_lse, void* qx_out,
+                                   float* row_max, long long* row_arg, float* row_lse, void* qx_out,
                                    float* xs_out, cudaStream_t stream) {
   if (M < 0) return -1;
   if (N <= 0 || N % 128) return -2;
@@ -1659,8 +1584,6 @@ int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, 
   void* scratch = nullptr;
   const int rc = static_scratch(&scratch);
   if (rc != 0) return rc;
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, 16, stream);
-  if (e != cudaSuccess) return (int)e;
   return b200_fp8_lmhead(x, M, K, wq, ws, N, vocab_offset, y, ldy, row_max, row_arg, row_lse,
                          qx_out, xs_out, scratch, STATIC_SCRATCH_BYTES, stream);
 }

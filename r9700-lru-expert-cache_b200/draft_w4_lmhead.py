@@ -265,7 +265,7 @@ def _run(x: torch.Tensor, wq: torch.Tensor, wsz: torch.Tensor, n: int, k: int,
     wsp = None
     if stats:
         mx = torch.empty(m, dtype=torch.float32, device=x.device)
-        arg = torch.empty(m, dtype=torch.int32, device=x.device)
+        arg = torch.empty(m, dtype=torch.int64, device=x.device)
         lse = torch.empty(m, dtype=torch.float32, device=x.device)
         wsp = workspace(x.device)
     rc = fn(_lib.ptr(x), 0 if x.dtype == torch.bfloat16 else 1, m, k, _lib.ptr(wq), _lib.ptr(wsz),
@@ -323,4 +323,4 @@ def gemm_w4a16_top(x: torch.Tensor, packed: PackedW4, vocab_offset: int = 0,
     logits = None
     if want_logits:
         logits = y if packed.n_pad == packed.n else y[:, :packed.n]
-    return logits, mx, arg.to(torch.int64), lse
+    return logits, mx, arg, lse

@@ -108,7 +108,7 @@ def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset
     if want_logits:
         y = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     mx = torch.empty(M, dtype=torch.float32, device=dev)
-    arg = torch.empty(M, dtype=torch.int32, device=dev)
+    arg = torch.empty(M, dtype=torch.int64, device=dev)
     lse = torch.empty(M, dtype=torch.float32, device=dev)
     qx = torch.empty(M, K, dtype=FP8, device=dev) if debug_quant else None
     xs = torch.empty(M, K // _BLK, dtype=torch.float32, device=dev) if debug_quant else None
@@ -118,7 +118,7 @@ def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset
         N if y is None else y.stride(0), _lib.ptr(mx), _lib.ptr(arg), _lib.ptr(lse),
         _lib.ptr(qx), _lib.ptr(xs), _lib.ptr(wsp), wsp.numel(), _lib.stream_ptr())
     _lib.check(rc, "b200_fp8_lmhead")
-    res = (y, mx, arg.to(torch.int64), lse)
+    res = (y, mx, arg, lse)
     return res + (qx, xs) if debug_quant else res
 
 

@@ -24,7 +24,7 @@ REL_FP8 = 3 * 3.7e-3 + 1e-4          # tests/k3/test_fp8sk.py:95 with the measur
 def _outputs(M, N, K, dev):
     return (torch.empty(M, N, device=dev, dtype=torch.bfloat16),
             torch.empty(M, device=dev, dtype=torch.float32),
-            torch.empty(M, device=dev, dtype=torch.int32),
+            torch.empty(M, device=dev, dtype=torch.int64),
             torch.empty(M, device=dev, dtype=torch.float32),
             torch.empty(M, K, device=dev, dtype=torch.uint8),
             torch.empty(M, K // 128, device=dev, dtype=torch.float32))
