@@ -155,9 +155,10 @@ B200_DEVINL uint4 lds128(uint32_t addr) {
 // ---- warp-level tensor-core MMAs (legacy mma.sync, used for the M <= 16 GEMVs) -------------
 
 // D(16x8 f32) += A(16x32 e4m3, row) * B(32x8 e4m3, col)
+// (Not volatile: pure register math, so the compiler may overlap it with the next loads.)
 B200_DEVINL void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                 uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -167,7 +168,7 @@ B200_DEVINL void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1, uint32_
 // D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
 B200_DEVINL void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

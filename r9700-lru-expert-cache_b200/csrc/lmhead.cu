@@ -206,27 +206,34 @@ __device__ void load_activation(const Params& p, char* sm, int rows_x, uint64_t*
 
 // ---- per-strip consumer math ----------------------------------------------------------------
 
+// Shared-memory operands are read through plain pointers (not volatile asm), so the compiler
+// can issue block j + 1's loads while block j's MMAs run; the stage's mbarrier wait, an asm
+// with a memory clobber, still orders them after the copy has landed.
 template <int NT8>
-__device__ __forceinline__ void fp8_stage(const Params& p, uint32_t stage, uint32_t xbase,
+__device__ __forceinline__ void fp8_stage(const Params& p, const char* stage, const char* xbase,
                                           const float* xs, int kb0, int nkb, int strip,
                                           float (&tot)[NT8][4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int KB = p.K / 128;
   const float* ws = static_cast<const float*>(p.wscale) + (long long)(strip >> 3) * KB;
   const float wsv = (lane < nkb) ? __ldg(ws + kb0 + lane) : 0.f;
-  const uint32_t c0 = ((t ^ g) & 7) * 16, c1 = (((t + 4) ^ g) & 7) * 16;
+  const int c0 = ((t ^ g) & 7) * 16, c1 = (((t + 4) ^ g) & 7) * 16;
+#pragma unroll 2
   for (int j = 0; j < nkb; ++j) {
     const float sw = __shfl_sync(0xffffffffu, wsv, j);
-    const uint32_t tile = stage + j * FP8_KB_BYTES;
-    const uint4 A0 = b200::lds128(tile + g * 128 + c0), A1 = b200::lds128(tile + g * 128 + c1);
-    const uint4 B0 = b200::lds128(tile + (g + 8) * 128 + c0), B1 = b200::lds128(tile + (g + 8) * 128 + c1);
+    const char* tile = stage + j * FP8_KB_BYTES;
+    const uint4 A0 = *reinterpret_cast<const uint4*>(tile + g * 128 + c0);
+    const uint4 A1 = *reinterpret_cast<const uint4*>(tile + g * 128 + c1);
+    const uint4 B0 = *reinterpret_cast<const uint4*>(tile + (g + 8) * 128 + c0);
+    const uint4 B1 = *reinterpret_cast<const uint4*>(tile + (g + 8) * 128 + c1);
     const uint32_t wa[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
     const uint32_t wb[8] = {B0.x, B0.y, B0.z, B0.w, B1.x, B1.y, B1.z, B1.w};
     const int kb = kb0 + j;
 #pragma unroll
     for (int nt = 0; nt < NT8; ++nt) {
-      const uint32_t xr = xbase + (8 * nt + g) * p.xs_stride + kb * 128;
-      const uint4 X0 = b200::lds128(xr + t * 16), X1 = b200::lds128(xr + (t + 4) * 16);
+      const char* xr = xbase + (8 * nt + g) * p.xs_stride + kb * 128;
+      const uint4 X0 = *reinterpret_cast<const uint4*>(xr + t * 16);
+      const uint4 X1 = *reinterpret_cast<const uint4*>(xr + (t + 4) * 16);
       const uint32_t xw[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -243,16 +250,17 @@ __device__ __forceinline__ void fp8_stage(const Params& p, uint32_t stage, uint3
 }
 
 template <int NT8>
-__device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32_t xbase, int kb0,
+__device__ __forceinline__ void w4_stage(const Params& p, const char* stage, const char* xbase, int kb0,
                                          int nkb, float (&tot)[NT8][4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const uint32_t szbase = stage + p.kps * W4_KB_BYTES;
+  const char* szbase = stage + p.kps * W4_KB_BYTES;
+#pragma unroll 2
   for (int j = 0; j < nkb; ++j) {
-    const uint32_t tile = stage + j * W4_KB_BYTES;
-    const uint4 A = b200::lds128(tile + (g * 4 + t) * 16);
-    const uint4 B = b200::lds128(tile + ((8 + g) * 4 + t) * 16);
-    const uint32_t szA = lds32(szbase + j * W4_SZ_BYTES + g * 4);
-    const uint32_t szB = lds32(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
+    const char* tile = stage + j * W4_KB_BYTES;
+    const uint4 A = *reinterpret_cast<const uint4*>(tile + (g * 4 + t) * 16);
+    const uint4 B = *reinterpret_cast<const uint4*>(tile + ((8 + g) * 4 + t) * 16);
+    const uint32_t szA = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + g * 4);
+    const uint32_t szB = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
     const float scA = __half2float(__ushort_as_half((unsigned short)(szA & 0xffffu)));
     const float scB = __half2float(__ushort_as_half((unsigned short)(szB & 0xffffu)));
     const uint32_t nzA = (szA >> 16) | (szA & 0xffff0000u);
@@ -272,7 +280,7 @@ __device__ __forceinline__ void w4_stage(const Params& p, uint32_t stage, uint32
       }
 #pragma unroll
       for (int nt = 0; nt < NT8; ++nt) {
-        const uint4 X = b200::lds128(xbase + (8 * nt + g) * p.xs_stride + (kb * 128 + 32 * w + 8 * t) * 2);
+        const uint4 X = *reinterpret_cast<const uint4*>(xbase + (8 * nt + g) * p.xs_stride + (kb * 128 + 32 * w + 8 * t) * 2);
         b200::mma_f16_16816(acc[nt], pa[0], pb[0], pa[1], pb[1], X.x, X.y);
         b200::mma_f16_16816(acc[nt], pa[2], pb[2], pa[3], pb[3], X.z, X.w);
       }
@@ -390,9 +398,8 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
     load_activation<KIND, NC>(p, sm, 8 * NT8, x_bar, deadline, &ok);
     consumer_bar<NC>();
     ok = ok && __all_sync(0xffffffffu, ok);
-    const uint32_t xbase = b200::smem_u32(sm + p.x_off);
+    const char* xbase = sm + p.x_off;
     const float* xs = reinterpret_cast<const float*>(sm + p.xs_off);
-    const uint32_t ring_u32 = b200::smem_u32(ring);
     const int g = lane >> 2, t = lane & 3;
     for (int ls = cw; ls < s1 - s0 && ok; ls += NC) {
       const int strip = s0 + ls;
@@ -406,7 +413,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
           ok = false;
           break;
         }
-        const uint32_t stage = ring_u32 + slot * p.stage_bytes;
+        const char* stage = ring + slot * p.stage_bytes;
         const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
         if (IS_W4)
           w4_stage<NT8>(p, stage, xbase, kb0, nkb, tot);
