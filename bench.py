@@ -7,7 +7,8 @@ epilogue on this rank's shard, then the all-gather combine of those triples. ``v
 algorithmic bytes of the whole head (weights N*K + block scales + bf16 activation + bf16
 logits + 12 B of statistics per token) / max-over-ranks step time, aggregated over all ranks
 (strong scaling: total work fixed). Weights are rotated through a pool larger than 2.5x the
-126 MB L2 so every step streams from HBM.
+126 MB L2 so every step streams from HBM. Each timed step is the replay of a CUDA graph that
+holds the step's launches (and at N > 1 the NCCL all-gather), one graph per weight copy.
 
 Secondary numbers in the same line: the expert-id-sharded LRU cache update (52 layers, the
 fused manage+align kernel, Zipf(1.1) routing) in us/layer; and on rank 0 at N=1 the other
@@ -145,13 +146,14 @@ def load_pkg():
     return importlib.import_module("r9700-lru-expert-cache_b200")
 
 
-def make_fp8_pool(P, n_rows: int, dev, seed: int):
-    """`copies` independent shards whose total exceeds POOL_BYTES."""
+def make_fp8_pool(P, n_rows: int, dev, seed: int, size_rows: int | None = None):
+    """`copies` independent shards whose total exceeds POOL_BYTES (counted on `size_rows`,
+    the largest shard, so that every rank builds -- and captures -- the same number)."""
     g = torch.Generator(device=dev).manual_seed(seed)
     w = (torch.randn(n_rows, K_HID, device=dev, generator=g) * 0.02).bfloat16()
     wq, ws = P.fp8_target_lmhead.pack_fp8_block(w)
     del w
-    copies = max(1, math.ceil(POOL_BYTES / (n_rows * K_HID)))
+    copies = max(1, math.ceil(POOL_BYTES / ((size_rows or n_rows) * K_HID)))
     pool = [(wq, ws)] + [(wq.clone(), ws.clone()) for _ in range(copies - 1)]
     return pool
 
@@ -383,48 +385,81 @@ def main():
     P = load_pkg()
     P.fp8_target_lmhead.available() or sys.exit("fp8 lm_head kernels unavailable")
 
-    r0, r1 = P.sharded.vocab_shards(N_VOCAB, world)[rank]
+    shards = P.sharded.vocab_shards(N_VOCAB, world)
+    r0, r1 = shards[rank]
     n_loc = r1 - r0
-    pool = make_fp8_pool(P, n_loc, dev, seed=100 + rank)
+    pool = make_fp8_pool(P, n_loc, dev, seed=100 + rank, size_rows=max(b - a for a, b in shards))
     torch.manual_seed(0)
     x = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
     y = torch.empty(M_ROWS, n_loc, dtype=torch.bfloat16, device=dev)
-    # per 64-token chunk: activation tiles, tcgen05 GEMM, split-block finish, statistics merge
-    launches_per_step = 4 * math.ceil(M_ROWS / 64)
+    # per 64-token chunk: activation tiles, tcgen05 GEMM, split-block finish, statistics merge;
+    # with N > 1 one peer-memory combine (two kernels around NCCL on the fallback path)
 
-    def step(i, kev=None):
+    def head(i):
         wq, ws = pool[i % len(pool)]
-        if kev is not None:
-            kev[0].record()
-        _, mx, arg, lse = P.fp8_target_lmhead.fp8_lmhead(x, wq, ws, vocab_offset=r0, out=y)
-        if kev is not None:
-            kev[1].record()
+        return P.fp8_target_lmhead.fp8_lmhead(x, wq, ws, vocab_offset=r0, out=y)
+
+    # N > 1: the statistics meet over NVLink peer memory in one kernel per rank (no NCCL call
+    # on the step); NCCL's all-gather path remains as the fallback where that is unavailable.
+    combiner = None
+    if world > 1:
+        try:
+            combiner = P.sharded.P2PCombiner(M_ROWS, dev)
+        except Exception as exc:                                  # noqa: BLE001
+            print(f"rank {rank}: peer-memory combine unavailable ({exc}); using NCCL", file=sys.stderr)
+
+    def step(i):
+        _, mx, arg, lse = head(i)
         if world > 1:
-            mx, arg, lse = P.sharded.combine_row_stats(mx, arg, lse)
+            mx, arg, lse = combiner(mx, arg, lse) if combiner else P.sharded.combine_row_stats(mx, arg, lse)
         return mx, arg, lse
 
     import torch.distributed as dist
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    # One CUDA graph per weight copy holds a whole step (the head's launches, and with N > 1
+    # the pack, NCCL all-gather and combine), so the timed loop measures the GPU, not the
+    # launch rate of the host; a second set holds the head alone for the kernel-only time.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(len(pool)):
+            step(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    def capture(fn, i):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn(i)
+        return gr
+    graphs = [capture(step, i) for i in range(len(pool))]
+    kgraphs = [capture(head, i) for i in range(len(pool))]
+    for i in range(args.warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    kevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.nvtx.range_push("timed")
         start.record()
         for i in range(args.steps):
-            step(i, kevs[i])
+            graphs[i % len(graphs)].replay()
         end.record()
         torch.cuda.synchronize(dev)
         torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
-    kern_us = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in kevs)
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record()
+    for i in range(args.steps):
+        kgraphs[i % len(kgraphs)].replay()
+    kb.record()
+    torch.cuda.synchronize(dev)
+    kern_us = ka.elapsed_time(kb) * 1e3 / args.steps
     t = torch.tensor([ms, kern_us], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -443,7 +478,7 @@ def main():
         wq, ws = pool[i % len(pool)]
         _, mx, arg, lse = P.fp8_target_lmhead.fp8_lmhead(xd, wq, ws, vocab_offset=r0, out=y)
         if world > 1:
-            mx, arg, lse = P.sharded.combine_row_stats(mx, arg, lse)
+            mx, arg, lse = combiner(mx, arg, lse) if combiner else P.sharded.combine_row_stats(mx, arg, lse)
         res_h.copy_(torch.stack([mx.double(), arg.double(), lse.double()], 1), non_blocking=True)
     for i in range(args.warmup):
         e2e_step(i)
@@ -477,6 +512,10 @@ def main():
     if world > 1:
         dist.barrier()
 
+    torch.cuda.synchronize(dev)
+    for gr in graphs + kgraphs:             # they hold NCCL work: release before the group goes
+        gr.reset()
+    del graphs, kgraphs
     if rank == 0:
         pk = peaks()
         per_launch_bytes = fp8_bytes(n_loc, K_HID, M_ROWS)
@@ -504,13 +543,15 @@ def main():
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                          "peak_source": pk["source"], "kernel_us": kern_us_max,
                          "kernel": "fp8_tc_kernel<64> (tcgen05); timed with its launch set "
-                                   "(act_tiles + tc + finish + merge), so achieved is a lower bound",
+                                   "(act_tiles + tc + finish + merge, one CUDA graph per step), "
+                                   "so achieved is a lower bound",
                          "bytes_per_launch_set": per_launch_bytes,
                          "read_control_GB_s": ceiling},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": M_ROWS * K_HID * 2, "d2h_bytes_per_step": M_ROWS * 24},
-            "gpu_launches": args.steps * launches_per_step,
+            "gpu_launches": args.steps * (4 * math.ceil(M_ROWS / 64) + (0 if world == 1 else 1 if combiner else 2)),
+            "combine": None if world == 1 else ("nvlink peer memory, 1 kernel" if combiner else "nccl all_gather"),
             "clocks": clk.summary(),
             "lru": lru,
             "ops": ops,

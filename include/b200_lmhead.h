@@ -67,6 +67,27 @@ int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, 
                                    float* row_max, long long* row_arg, float* row_lse, void* qx_out,
                                    float* xs_out, cudaStream_t stream);
 
+/* Vocabulary-sharded combine (new; the reference gathers full logits instead): pack this
+ * rank's (max, argmax, logsumexp) as [M][3] float64, all-gather them (NCCL), then combine the
+ * `world` blocks (rank-major, shards in vocabulary order) into the global max, first argmax
+ * and logsumexp. Returns 0, -1 bad sizes, else the launch's cudaError_t. */
+int b200_pack_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
+                        double* out, cudaStream_t stream);
+int b200_combine_row_stats(const double* gathered, int world, int M, float* row_max, long long* row_arg,
+                           float* row_lse, cudaStream_t stream);
+
+/* The same combine as ONE kernel over NVLink peer memory (no NCCL call): each rank stores its
+ * packed triples into every rank's peer-addressable buffer (b200_p2p_combine_bytes each; e.g.
+ * torch symmetric memory), raises an arrival counter there with a system-scope release, waits
+ * (bounded, 1 s; timeout sets error word 2) for all ranks and combines. `peers` is a device
+ * array of the world buffer pointers as this GPU addresses them; `counter` a device uint64
+ * starting at 0; buffers' counters zeroed before the first call; all ranks make the same calls. */
+long long b200_p2p_combine_bytes(int world, int M_cap);
+int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
+                               int M_cap, void* const* peers, int rank, int world,
+                               unsigned long long* counter, float* out_max, long long* out_arg,
+                               float* out_lse, cudaStream_t stream);
+
 /* The closed fp8hip GEMM's ABI (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K]
  * and fp32 xs [M, K/128], packed w / ws, bf16 y [M, N]. */
 int fp8hip_gemm_w8a8_launch(void* qx, void* w, void* xs, void* ws, void* y, int M, int N, int K,

@@ -32,6 +32,11 @@ LMHEAD_PROTOS = {
                                 c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "b200_fp8_lmhead_static_scratch": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_ll, c_vp,
                                                c_ll, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "b200_pack_row_stats": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
+    "b200_combine_row_stats": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "b200_p2p_combine_bytes": (c_ll, [c_int, c_int]),
+    "b200_p2p_combine_row_stats": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp,
+                                           c_vp, c_vp, c_vp]),
     "fp8hip_gemm_w8a8_launch": (c_int, [c_vp] * 5 + [c_int] * 3 + [c_vp]),
     "hcq_gemm_fp8blk_nt_m16": (c_int, [c_vp] * 5 + [c_int] * 6 + [c_vp]),
     "hcq_gemm_fp8blk_nt_m16_max_m": (c_int, []),

@@ -1146,6 +1146,123 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) 
   }
 }
 
+// ---- vocabulary-sharded combine of the row statistics ---------------------------------------
+// Each rank's (max, argmax, logsumexp) per token is packed as three float64 (exact for the
+// index), all-gathered by NCCL, and combined: global max; argmax of the first rank attaining
+// it (shards are in vocabulary order, so this is the first global index); logsumexp =
+// max + log sum_r exp(lse_r - max).
+__global__ void pack_row_stats_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
+                                      const float* __restrict__ lse, int M, double* __restrict__ out) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  out[3 * m] = (double)mx[m];
+  out[3 * m + 1] = (double)arg[m];
+  out[3 * m + 2] = (double)lse[m];
+}
+
+__global__ void combine_row_stats_kernel(const double* __restrict__ g, int world, int M, float* __restrict__ mx,
+                                         long long* __restrict__ arg, float* __restrict__ lse) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  double gm = g[3 * m];
+  int first = 0;
+  for (int r = 1; r < world; ++r) {
+    const double v = g[((long long)r * M + m) * 3];
+    if (v > gm) {
+      gm = v;
+      first = r;
+    }
+  }
+  double s = 0.0;
+  for (int r = 0; r < world; ++r) s += exp(g[((long long)r * M + m) * 3 + 2] - gm);
+  if (mx) mx[m] = (float)gm;
+  if (arg) arg[m] = (long long)g[((long long)first * M + m) * 3 + 1];
+  if (lse) lse[m] = (float)(gm + log(s));
+}
+
+// ---- the same combine over NVLink peer memory, one kernel per rank ---------------------------
+// Every rank owns a buffer in memory all ranks can address (torch symmetric memory):
+// [2 parities][world][M_cap][3] float64 of packed triples, then [world] uint64 arrival counters.
+// Call k (k = this rank's device counter, equal on every rank since all make the same calls):
+// each token's thread stores the rank's triple into slot [k & 1][rank] of EVERY rank's buffer
+// (plain stores over NVLink), then thread 0 publishes arrival k + 1 into every rank's counter
+// [rank] with a system-scope release, waits -- bounded by %globaltimer -- until its own
+// counters all reach k + 1, and the block combines from its own buffer. Double-buffering by
+// parity makes reuse safe: a rank can only write parity k & 1 again at call k + 2, which needs
+// every rank's arrival k + 1, i.e. every rank has finished call k. No NCCL call, no second launch.
+constexpr long long P2P_WAIT_NS = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
+                                                          const float* __restrict__ lse, int M, int M_cap,
+                                                          char* const* __restrict__ peers, int rank, int world,
+                                                          unsigned long long* __restrict__ counter,
+                                                          float* __restrict__ out_mx, long long* __restrict__ out_arg,
+                                                          float* __restrict__ out_lse) {
+  __shared__ unsigned long long s_k;
+  if (threadIdx.x == 0) s_k = *counter;
+  __syncthreads();
+  const unsigned long long k = s_k;
+  const long long data_bytes = 2LL * world * M_cap * 3 * 8;
+  const int par = (int)(k & 1);
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const double a = (double)mx[m], b = (double)arg[m], c = (double)lse[m];
+    for (int q = 0; q < world; ++q) {
+      double* dst = reinterpret_cast<double*>(peers[q]) + (((long long)par * world + rank) * M_cap + m) * 3;
+      dst[0] = a;
+      dst[1] = b;
+      dst[2] = c;
+    }
+  }
+  __threadfence_system();                   // this thread's peer stores, before the arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < world; ++q)
+      st_release_sys(reinterpret_cast<unsigned long long*>(peers[q] + data_bytes) + rank, k + 1);
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(peers[rank] + data_bytes);
+    const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
+    bool ok = true;
+    for (int q = 0; q < world && ok; ++q) {
+      uint32_t n = 0;
+      while (ld_acquire_sys(mine + q) < k + 1) {
+        if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) atomicExch(&g_lmhead_err, 2);
+    *counter = k + 1;
+  }
+  __syncthreads();
+  const double* g = reinterpret_cast<const double*>(peers[rank]) + (long long)par * world * M_cap * 3;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    double gm = __ldcg(g + (long long)m * 3);
+    int first = 0;
+    for (int r = 1; r < world; ++r) {
+      const double v = __ldcg(g + ((long long)r * M_cap + m) * 3);
+      if (v > gm) {
+        gm = v;
+        first = r;
+      }
+    }
+    double sum = 0.0;
+    for (int r = 0; r < world; ++r) sum += exp(__ldcg(g + ((long long)r * M_cap + m) * 3 + 2) - gm);
+    if (out_mx) out_mx[m] = (float)gm;
+    if (out_arg) out_arg[m] = (long long)__ldcg(g + ((long long)first * M_cap + m) * 3 + 1);
+    if (out_lse) out_lse[m] = (float)(gm + log(sum));
+  }
+}
+
 // ---- read-only stream control (hcq_stream_probe, hcq_fp8skinny.hip:206-224) -----------------
 __global__ void __launch_bounds__(256) stream_probe_kernel(const uint4* __restrict__ w, size_t n16,
                                                            unsigned* __restrict__ out) {
@@ -1468,6 +1585,47 @@ int hcq_gemm_fp8blk_nt_m16(void* a, void* as, void* w, void* ws, void* c, int M,
 }
 
 int hcq_gemm_fp8blk_nt_m16_max_m(void) { return MAXM; }
+
+// Pack this rank's per-token (max, argmax, logsumexp) as [M][3] float64 for the all-gather.
+int b200_pack_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
+                        double* out, cudaStream_t stream) {
+  if (M < 0) return -1;
+  if (M == 0) return 0;
+  pack_row_stats_kernel<<<(M + 127) / 128, 128, 0, stream>>>(row_max, row_arg, row_lse, M, out);
+  return (int)cudaGetLastError();
+}
+
+// Combine `world` gathered [M][3] float64 blocks (rank-major, shards in vocabulary order) into
+// the global per-token max, first argmax and logsumexp; each output is nullable.
+int b200_combine_row_stats(const double* gathered, int world, int M, float* row_max, long long* row_arg,
+                           float* row_lse, cudaStream_t stream) {
+  if (M < 0 || world <= 0) return -1;
+  if (M == 0) return 0;
+  combine_row_stats_kernel<<<(M + 127) / 128, 128, 0, stream>>>(gathered, world, M, row_max, row_arg, row_lse);
+  return (int)cudaGetLastError();
+}
+
+// Bytes of the per-rank peer-addressable buffer b200_p2p_combine_row_stats needs.
+long long b200_p2p_combine_bytes(int world, int M_cap) {
+  return 2LL * world * M_cap * 3 * 8 + (long long)world * 8;
+}
+
+// The vocabulary-sharded combine in one kernel over NVLink peer memory (see above). `peers` is
+// a DEVICE array of `world` pointers, peers[q] = rank q's buffer as this GPU addresses it (its
+// counters zeroed before the first call); `counter` is this rank's device call counter (starts
+// at 0). Every rank must make the same sequence of calls. A peer that does not arrive within
+// 1 s sets the error word to 2 (b200_lmhead_error) and the outputs are not meaningful.
+// Returns 0, -1 bad sizes, else the launch's cudaError_t.
+int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
+                               int M_cap, void* const* peers, int rank, int world,
+                               unsigned long long* counter, float* out_max, long long* out_arg,
+                               float* out_lse, cudaStream_t stream) {
+  if (M < 0 || M > M_cap || world <= 0 || rank < 0 || rank >= world) return -1;
+  p2p_combine_kernel<<<1, 128, 0, stream>>>(row_max, row_arg, row_lse, M, M_cap,
+                                            reinterpret_cast<char* const*>(peers), rank, world, counter,
+                                            out_max, out_arg, out_lse);
+  return (int)cudaGetLastError();
+}
 
 // Read-only control: streams `bytes` from w with 16-byte loads over `wgs` CTAs of 256.
 int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream) {

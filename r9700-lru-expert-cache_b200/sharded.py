@@ -54,17 +54,71 @@ def _combine(mx: torch.Tensor, ar: torch.Tensor, ls: torch.Tensor):
 
 def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, group=None):
     """All-gather this rank's per-row (max, argmax, lse) and combine: [M, 3] float64 per
-    rank (24 B/row) in one collective; every rank returns the global triple."""
+    rank (24 B/row) in one collective; every rank returns the global triple. On CUDA the
+    pack and the combine are one small kernel each (b200_pack_row_stats /
+    b200_combine_row_stats) around NCCL's all-gather, so the step stays three launches."""
     world = dist.get_world_size(group)
-    local = torch.stack([mx.double(), arg.double(), lse.double()], dim=1).contiguous()
-    if local.is_cuda:
-        gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    if mx.is_cuda:
+        from . import _lib
+        lib = _lib.lmhead()
+        M = mx.numel()
+        arg64 = arg if arg.dtype == torch.int64 else arg.to(torch.int64)
+        local = torch.empty(M, 3, dtype=torch.float64, device=mx.device)
+        _lib.check(lib.b200_pack_row_stats(_lib.ptr(mx), _lib.ptr(arg64), _lib.ptr(lse), M, _lib.ptr(local),
+                                           _lib.stream_ptr()), "b200_pack_row_stats")
+        gathered = torch.empty((world, M, 3), dtype=torch.float64, device=mx.device)
         dist.all_gather_into_tensor(gathered, local, group=group)
-    else:                                   # gloo (host-side tests of the combine)
-        parts = [torch.empty_like(local) for _ in range(world)]
-        dist.all_gather(parts, local, group=group)
-        gathered = torch.stack(parts)
+        gm = torch.empty(M, dtype=torch.float32, device=mx.device)
+        ga = torch.empty(M, dtype=torch.int64, device=mx.device)
+        gl = torch.empty(M, dtype=torch.float32, device=mx.device)
+        _lib.check(lib.b200_combine_row_stats(_lib.ptr(gathered), world, M, _lib.ptr(gm), _lib.ptr(ga),
+                                              _lib.ptr(gl), _lib.stream_ptr()), "b200_combine_row_stats")
+        return gm, ga, gl
+    local = torch.stack([mx.double(), arg.double(), lse.double()], dim=1).contiguous()
+    parts = [torch.empty_like(local) for _ in range(world)]     # gloo (host-side tests)
+    dist.all_gather(parts, local, group=group)
+    gathered = torch.stack(parts)
     return _combine(gathered[:, :, 0], gathered[:, :, 1].to(torch.int64), gathered[:, :, 2])
+
+
+class P2PCombiner:
+    """combine_row_stats as ONE kernel over NVLink peer memory (b200_p2p_combine_row_stats):
+    each rank stores its packed (max, argmax, lse) triples straight into every rank's buffer
+    (torch symmetric memory), raises an arrival counter there, waits (bounded) for all ranks
+    and combines -- no NCCL call, no host involvement, so it can sit in a CUDA graph. Every
+    rank must make the same sequence of calls; M <= M_cap."""
+
+    def __init__(self, M_cap: int, device: torch.device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _lib
+        self._lib = _lib
+        self.lib = _lib.lmhead()
+        group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.M_cap = M_cap
+        nbytes = int(self.lib.b200_p2p_combine_bytes(self.world, M_cap))
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group)
+        ptrs = [self.handle.get_remote_tensor(q, (nbytes,), torch.uint8).data_ptr() for q in range(self.world)]
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)                 # every rank's counters are zero before any arrival
+
+    def __call__(self, mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor):
+        L = self._lib
+        M = mx.numel()
+        arg64 = arg if arg.dtype == torch.int64 else arg.to(torch.int64)
+        gm = torch.empty(M, dtype=torch.float32, device=mx.device)
+        ga = torch.empty(M, dtype=torch.int64, device=mx.device)
+        gl = torch.empty(M, dtype=torch.float32, device=mx.device)
+        L.check(self.lib.b200_p2p_combine_row_stats(L.ptr(mx), L.ptr(arg64), L.ptr(lse), M, self.M_cap,
+                                                    L.ptr(self.peers), self.rank, self.world, L.ptr(self.counter),
+                                                    L.ptr(gm), L.ptr(ga), L.ptr(gl), L.stream_ptr()),
+                "b200_p2p_combine_row_stats")
+        return gm, ga, gl
 
 
 def shard_fp8_head(wq: torch.Tensor, ws: torch.Tensor, rank: int, world: int):

@@ -111,6 +111,30 @@ def test_fp8_vocab_shards_combine(cuda):
     assert torch.equal(ca, arg) and torch.allclose(cm, mx) and torch.allclose(cl, lse, atol=1e-5)
 
 
+def test_combine_kernels_match_reference(cuda):
+    """b200_pack_row_stats + b200_combine_row_stats (the CUDA side of combine_row_stats) give
+    the torch combine's result on the same gathered triples, ties going to the first rank."""
+    L = P._lib
+    lib = L.lmhead()
+    W, M = 3, 37
+    g = torch.Generator(device=cuda).manual_seed(5)
+    mx = torch.randn(W, M, device=cuda, generator=g)
+    mx[1, :5] = mx[0, :5]
+    mx[2, 5:9] = mx[1, 5:9]
+    arg = torch.randint(0, 1 << 20, (W, M), device=cuda, generator=g, dtype=torch.int64)
+    lse = mx + torch.rand(W, M, device=cuda, generator=g)
+    packed = torch.empty(W, M, 3, dtype=torch.float64, device=cuda)
+    for r in range(W):
+        assert lib.b200_pack_row_stats(L.ptr(mx[r]), L.ptr(arg[r]), L.ptr(lse[r]), M, L.ptr(packed[r]),
+                                       L.stream_ptr()) == 0
+    gm = torch.empty(M, device=cuda)
+    ga = torch.empty(M, dtype=torch.int64, device=cuda)
+    gl = torch.empty(M, device=cuda)
+    assert lib.b200_combine_row_stats(L.ptr(packed), W, M, L.ptr(gm), L.ptr(ga), L.ptr(gl), L.stream_ptr()) == 0
+    rm, ra, rl = P.sharded._combine(packed[:, :, 0], packed[:, :, 1].to(torch.int64), packed[:, :, 2])
+    assert torch.equal(ga, ra) and torch.equal(gm, rm) and torch.allclose(gl, rl, atol=1e-6)
+
+
 def test_fp8_graph_replay(cuda):
     N, K, M = 4096, 2560, 5
     wq, ws, _ = _fp8_weight(N, K, 2, cuda)
