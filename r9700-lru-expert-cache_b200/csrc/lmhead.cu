@@ -46,7 +46,9 @@
 namespace {
 
 constexpr int NC_FP8 = 4;                // consumer warps of the FP8 GEMV
-constexpr int NC_W4 = 8;                 // consumer warps of the W4 GEMV (more ALU per byte)
+constexpr int NC_W4 = 8;                 // consumer warps of the W4 GEMV (more ALU per byte), M <= 8
+constexpr int NC_W4_WIDE = 6;            // ... and for 8 < M <= 16, where the larger activation
+                                         // region leaves fewer stages (see plan())
 constexpr int MAXM = 16;                 // tokens per GEMV launch
 constexpr int SMEM_CAP = 227 * 1024;
 constexpr int MAX_STAGES = 16;
@@ -1291,6 +1293,11 @@ int num_sms() {
 }
 
 // Fill in the GEMV's shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
+// Consumer warp c takes strips c, c + NC, ... of CH = ceil(KB / kps) stages each, and waits on
+// a stage slot by the parity of its round; the wait is unambiguous only while the slot's
+// previous round has already been issued, which holds when nstage >= (NC - 1) * CH + 1 (the
+// producer issues in order, and a consumer starting a strip has finished a stage at most
+// (NC - 1) * CH + 1 positions earlier). Plans below that bound are rejected.
 int plan(Params& p, bool is_w4, int nt8, int nc) {
   const int KB = p.K / 128;
   const int rows_x = 8 * nt8;
@@ -1299,13 +1306,13 @@ int plan(Params& p, bool is_w4, int nt8, int nc) {
   p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
   const int fixed = p.x_off + rows_x * p.xs_stride;
   const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
-  // Whole-strip stages (one bulk copy of weights per stage), as deep a ring as fits.
-  const int want = 4;
+  // The largest stages (fewest, biggest bulk copies) that still give a safe ring.
   for (int kps = min(KB, 24); kps >= 1; --kps) {
+    const int ch = (KB + kps - 1) / kps;
     const int sb = (kps * per_kb + 127) & ~127;
     const int ring_off = (fixed + 127) & ~127;
     const int nstage = min(MAX_STAGES, (SMEM_CAP - ring_off) / sb);
-    if (nstage >= want || (kps == 1 && nstage >= 2)) {
+    if (nstage >= max(2, (nc - 1) * ch + 1)) {
       p.kps = kps;
       p.stage_bytes = sb;
       p.nstage = nstage;
@@ -1338,7 +1345,7 @@ int launch_ex(void (*kern)(Exp...), dim3 grid, dim3 block, int smem, cudaStream_
 template <int KIND, int NT8, bool STATS>
 int launch_one(Params p, cudaStream_t stream) {
   constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
-  constexpr int NC = IS_W4 ? NC_W4 : NC_FP8;
+  constexpr int NC = IS_W4 ? (NT8 == 1 ? NC_W4 : NC_W4_WIDE) : NC_FP8;
   const int smem = plan(p, IS_W4, NT8, NC);
   if (smem < 0) return -8;
   auto kern = gemv_kernel<KIND, NT8, STATS, NC>;

@@ -78,9 +78,11 @@ def test_fp8_prequantized_abi(cuda):
     assert rc == 0 and torch.equal(y, y2)
 
 
-@pytest.mark.parametrize("M", [1, 5, 20])
+@pytest.mark.parametrize("M", [1, 5, 16, 20, 64])
 def test_fp8_fused_baseline_shape(cuda, M):
-    """Full target head: W ~N(0,0.02) [151936, 2560], x ~N(0,1)."""
+    """Full target head: W ~N(0,0.02) [151936, 2560], x ~N(0,1). At this size every CTA streams
+    many strips, so the ring's slots turn over many times; the device error word (a pipeline
+    wait that ran out) must stay clear."""
     N, K = 151936, 2560
     wq, ws, wdq = _fp8_weight(N, K, 0, cuda)
     x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16, generator=torch.Generator(device=cuda).manual_seed(M))
@@ -93,6 +95,7 @@ def test_fp8_fused_baseline_shape(cuda, M):
     dlp = ((y.float() - lse.unsqueeze(1)) - lp.float()).abs().max().item()
     print(f"FP8 N={N} M={M}: rel {rel:.3e}, max|dlogit| {d.max().item():.3e}, max|dlogprob| {dlp:.3e}")
     assert rel < REL_FP8
+    assert P._lib.lmhead().b200_lmhead_error(1) == 0
     del wdq, ref
 
 
@@ -222,9 +225,11 @@ def test_w4_reference_c_abi_f16(cuda):
     assert torch.equal(c, W4.gemm_w4a16(x, p))
 
 
-def test_w4_baseline_shape(cuda):
-    """Full draft head: x [4, 2560] ~N(0,1), W ~N(0,0.02) [151936, 2560]."""
-    n, k, M = 151936, 2560, 4
+@pytest.mark.parametrize("M", [4, 16])
+def test_w4_baseline_shape(cuda, M):
+    """Full draft head: x [M, 2560] ~N(0,1), W ~N(0,0.02) [151936, 2560]; M=16 takes the wider
+    activation region (fewer ring stages); the device error word must stay clear."""
+    n, k = 151936, 2560
     w = (torch.randn(n, k, device=cuda, generator=torch.Generator(device=cuda).manual_seed(0)) * 0.02).bfloat16()
     p = W4.pack_w4a16(w)
     del w
@@ -238,6 +243,7 @@ def test_w4_baseline_shape(cuda):
     gap = Q.top2_gap(r)
     print(f"W4 N={n} M={M}: rel-Frobenius {rel:.3e}, top2 gaps {gap.tolist()}")
     assert rel < 5e-3
+    assert P._lib.lmhead().b200_lmhead_error(1) == 0
     for m in range(M):
         if gap[m] > 1e-3:
             assert int(arg[m]) == int(rarg[m])
