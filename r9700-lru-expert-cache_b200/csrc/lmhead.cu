@@ -1459,8 +1459,11 @@ int launch_tc(const Params& p, const uint8_t* qx_in, const float* xs_in, cudaStr
 }
 
 // Runs M in token chunks, one weight pass each. With a workspace, FP8 takes 64-token chunks:
-// above 16 tokens the tcgen05 kernel, at most 16 the GEMV fed by act_rows_kernel (both as
+// from TC_MIN_M tokens the tcgen05 kernel, below it the GEMV fed by act_rows_kernel (both as
 // programmatic dependents of their activation kernel). Without one, 16-token GEMV chunks.
+// (From 9 tokens the GEMV's warp MMAs, two n-tiles per strip, cost more than the tcgen05
+// pipeline: 90 against 82 us for the 151936 x 2560 head at M = 12-16.)
+constexpr int TC_MIN_M = 9;
 template <int KIND>
 int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
   const int M = p.M, KB = p.K / 128;
@@ -1481,7 +1484,7 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
     if (p.qx_out) q.qx_out = p.qx_out + (long long)m0 * p.K;
     if (p.xs_out) q.xs_out = p.xs_out + (long long)m0 * KB;
     int rc;
-    if (tc_ok && q.M > MAXM) {
+    if (tc_ok && q.M >= TC_MIN_M) {
       const uint8_t* qx_in = (KIND == FP8_PREQ) ? static_cast<const uint8_t*>(q.x) : nullptr;
       rc = stats ? launch_tc<true>(q, qx_in, q.xs_in, stream) : launch_tc<false>(q, qx_in, q.xs_in, stream);
     } else if (KIND == FP8_QUANT && have_ws && (long long)MAXM * p.K <= QR_CAP) {

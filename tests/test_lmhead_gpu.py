@@ -45,7 +45,7 @@ def _check_stats(tag, logits_ref, mx, arg, lse, offset=0):
     return lp
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 12, 16, 20, 64])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 12, 16, 20, 33, 64])
 def test_fp8_fused_small_shape(cuda, M):
     N, K = 8192, 2560
     wq, ws, wdq = _fp8_weight(N, K, N * 7 + K, cuda)
