@@ -138,6 +138,44 @@ def cpu_baseline_fp8(sample_rows: int = 16384, reps: int = 3) -> dict:
             "seconds_per_sample": t}
 
 
+def cpu_baseline_ops() -> dict:
+    """The reference's CPU forms of the other ops on this box's host cores, bounded samples:
+    W4 head = dequantize (unpack) + fp32 matmul (the reference's M > 64 fallback form) on a
+    vocabulary sample; LRU = the numpy reference model's manage step per layer; SiLU-quant =
+    the torch eager restatement at the decode shape."""
+    from oracle import lru_oracle as LO
+    from oracle import quant_oracle as Q
+    res = {}
+    torch.manual_seed(0)
+    rows = 16384
+    w = (torch.randn(rows, K_HID) * 0.02).bfloat16()
+    q, sc, z = Q.quantize_w4(w)
+    x = torch.randn(4, K_HID).bfloat16()
+    t0 = time.perf_counter()
+    wdq = Q.w4_dequant(q, sc, z)
+    y = x.float().half().float() @ wdq.t()
+    Q.row_stats(y)
+    t = time.perf_counter() - t0
+    res["w4_lmhead_M4"] = {"GB_s": w4_bytes(rows, K_HID, 4) / t / 1e9,
+                           "sample": f"{rows} of {N_VOCAB} rows: unpack + fp32 matmul + row stats"}
+    rng = np.random.default_rng(7)
+    st = LO.warm_state(E_EXPERTS, S_SLOTS, sorted(rng.choice(E_EXPERTS, S_SLOTS, replace=False).tolist()),
+                       stamps=rng.permutation(S_SLOTS) + 1, step=S_SLOTS)
+    routes = [LO.zipf_rows(rng, E_EXPERTS, 5, TOPK).ravel() for _ in range(LAYERS)]
+    t0 = time.perf_counter()
+    for r in routes:
+        LO.manage(st, r, int(S_SLOTS * 0.5), 64)
+    res["lru_manage_us_per_layer"] = (time.perf_counter() - t0) / LAYERS * 1e6
+    xs = torch.randn(8, 1024).bfloat16()
+    Q.silu_mul_quant(xs)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        Q.silu_mul_quant(xs)
+    res["silu_mul_quant_T8_d512_us"] = (time.perf_counter() - t0) / 20 * 1e6
+    res["cores"] = torch.get_num_threads()
+    return res
+
+
 # ---------------------------------------------------------------------------------------
 # GPU pieces
 # ---------------------------------------------------------------------------------------
@@ -279,6 +317,17 @@ def ops_bench(P, dev) -> dict:
     xs = torch.randn(8, 1024, device=dev, dtype=torch.bfloat16)
     us = time_graph(lambda: P.fused_silu_mul_quant.silu_mul_quant(xs, torch.float8_e4m3fn), 200, dev)
     res["silu_mul_quant_T8_d512"] = {"us_per_call": us, "bytes": 8 * 2048 + 8 * 512 + 8 * 4}
+    # large-T sweep point: [8192, 2x512] bf16 inputs rotated through a pool larger than L2
+    T, d = 8192, 512
+    bufs = [torch.randn(T, 2 * d, device=dev, dtype=torch.bfloat16) for _ in range(8)]
+    it = {"i": 0}
+
+    def silu_big():
+        P.fused_silu_mul_quant.silu_mul_quant(bufs[it["i"] % len(bufs)], torch.float8_e4m3fn)
+        it["i"] += 1
+    us = time_graph(silu_big, 2 * len(bufs), dev)
+    nb = T * 2 * d * 2 + T * d + T * 4
+    res[f"silu_mul_quant_T{T}_d{d}"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
     return res
 
 
@@ -528,6 +577,7 @@ def main():
             if key in tj:
                 traffic = tj[key]
         cpu = cpu_baseline_fp8() if world == 1 else None
+        cpu_ops = cpu_baseline_ops() if (world == 1 and not args.no_extras) else None
         line = {
             "metric": "FP8 target lm_head throughput (algorithmic HBM GB/s, vocab-sharded)",
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -555,6 +605,7 @@ def main():
             "clocks": clk.summary(),
             "lru": lru,
             "ops": ops,
+            "ops_cpu_baseline": cpu_ops,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

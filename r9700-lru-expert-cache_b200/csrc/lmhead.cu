@@ -1285,11 +1285,33 @@ __global__ void __launch_bounds__(256) stream_probe_kernel(const uint4* __restri
 
 // ---- host side -------------------------------------------------------------------------------
 
+// ---- per-device host state, set up on first use (a call then costs launches, not queries) ----
+constexpr int HOST_MAX_DEVICES = 64;
+
+int current_device() {
+  int dev = 0;
+  return (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < HOST_MAX_DEVICES) ? dev : 0;
+}
+
 int num_sms() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
-  return n;
+  static int cached[HOST_MAX_DEVICES] = {};
+  const int dev = current_device();
+  if (cached[dev] <= 0) {
+    int n = 0;
+    cached[dev] = (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Raise a kernel's dynamic shared-memory limit to the full 227 KB once per device, so later
+// launches with any plan need no attribute call. `done` is the kernel's own flag array.
+int allow_full_smem(const void* kern, bool (&done)[HOST_MAX_DEVICES]) {
+  const int dev = current_device();
+  if (done[dev]) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_CAP);
+  if (e != cudaSuccess) return (int)e;
+  done[dev] = true;
+  return 0;
 }
 
 // Fill in the GEMV's shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
@@ -1349,8 +1371,9 @@ int launch_one(Params p, cudaStream_t stream) {
   const int smem = plan(p, IS_W4, NT8, NC);
   if (smem < 0) return -8;
   auto kern = gemv_kernel<KIND, NT8, STATS, NC>;
-  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return (int)e;
+  static bool smem_set[HOST_MAX_DEVICES] = {};
+  const int e = allow_full_smem((const void*)kern, smem_set);
+  if (e != 0) return e;
   const int grid = min(p.N / 16, num_sms());
   const int rc = launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
   if (rc != 0 || !STATS) return rc;
@@ -1399,7 +1422,7 @@ int plan_tc(Params& p, int tpad) {
 // 128x128 tiles of two consecutive 128-row blocks at one 128-K block, each landing as
 // [128 rows][128 B] already in the 128-byte-swizzled order (the pack stores it that way; the
 // copy itself does not swizzle). Strips beyond N read as zeros.
-int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
+int encode_strip_map(CUtensorMap* m, const void* w, int N, int K) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -1418,6 +1441,32 @@ int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -12;
+}
+
+// The tensor map of a weight depends only on (address, N, K): keep the last few encodings, so
+// repeated calls on the same head skip the encode.
+int make_strip_map(CUtensorMap* m, const void* w, int N, int K) {
+  struct Entry {
+    const void* w;
+    int N, K;
+    CUtensorMap map;
+  };
+  constexpr int SLOTS = 16;
+  static Entry cache[SLOTS];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].w == w && cache[i].N == N && cache[i].K == K) {
+      *m = cache[i].map;
+      return 0;
+    }
+  const int rc = encode_strip_map(m, w, N, K);
+  if (rc != 0) return rc;
+  cache[next] = Entry{w, N, K, *m};
+  next = (next + 1) % SLOTS;
+  used = used < SLOTS ? used + 1 : SLOTS;
+  return 0;
 }
 
 template <int TPAD, bool STATS>
@@ -1439,8 +1488,9 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
                      p.K, TPAD, qt, xt, p.qx_out, p.xs_out);
   if (rc != 0) return rc;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
-  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return (int)e;
+  static bool smem_set[HOST_MAX_DEVICES] = {};
+  const int e = allow_full_smem((const void*)kern, smem_set);
+  if (e != 0) return e;
   p.pdl = 1;
   const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
   const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
