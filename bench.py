@@ -314,6 +314,23 @@ def ops_bench(P, dev) -> dict:
     gbs = w4_bytes(packed[0].n_pad, K_HID, 4) / us / 1e3
     res["w4_lmhead_M4"] = {"us_per_call": us, "GB_s": gbs, "frac_hbm": gbs / pk}
     del packed
+    # the symmetric int4 format with bf16 group scales (2 B per group instead of 4)
+    w = (torch.randn(N_VOCAB, K_HID, device=dev) * 0.02).bfloat16()
+    ps = [P.draft_w4_lmhead.pack_w4a16_sym(w)]
+    del w
+    for _ in range(max(1, math.ceil(POOL_BYTES / ps[0].nbytes)) - 1):
+        p0 = ps[0]
+        ps.append(P.draft_w4_lmhead.PackedW4(p0.wq.clone(), p0.wsz.clone(), p0.n, p0.n_pad, p0.k, True))
+    it = {"i": 0}
+
+    def w4scall():
+        q = ps[it["i"] % len(ps)]
+        it["i"] += 1
+        P.draft_w4_lmhead.gemm_w4a16_top(x, q)
+    us = time_graph(w4scall, 2 * len(ps), dev)
+    nb = ps[0].n_pad * K_HID // 2 + ps[0].n_pad * (K_HID // 128) * 2 + 4 * K_HID * 2 + 4 * ps[0].n_pad * 2
+    res["w4sym_lmhead_M4"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
+    del ps
     xs = torch.randn(8, 1024, device=dev, dtype=torch.bfloat16)
     us = time_graph(lambda: P.fused_silu_mul_quant.silu_mul_quant(xs, torch.float8_e4m3fn), 200, dev)
     res["silu_mul_quant_T8_d512"] = {"us_per_call": us, "bytes": 8 * 2048 + 8 * 512 + 8 * 4}

@@ -116,6 +116,14 @@ int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, con
                    float* row_max, long long* row_arg, float* row_lse, void* workspace,
                    long long workspace_bytes, cudaStream_t stream);
 
+/* b200_w4_lmhead for the symmetric int4 format with bf16 group scales (the draft head's
+ * configuration in this project's benchmark; the reference itself packs f16 scale + zero):
+ * `wscale` bf16 [N_pad/16, K/128, 16], a code q in 0..15 means (q - 8) * scale. Same codes. */
+int b200_w4_lmhead_sym(const void* x, int x_dtype, int M, int K, const void* wq, const void* wscale,
+                       int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                       float* row_max, long long* row_arg, float* row_lse, void* workspace,
+                       long long workspace_bytes, cudaStream_t stream);
+
 /* r4d_gemm_w4a16_nt_m64 (ABI bound at kernels/draft_w4_lmhead.py:118-127): f16 a [M, K],
  * M <= 64, packed wq / wsz, bf16 c [M, N] with N = N_pad. WV/SK/MB/NPW/NT are the gfx1201
  * launch knobs, accepted and ignored. Returns void like the reference; the status of the

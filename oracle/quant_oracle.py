@@ -195,6 +195,31 @@ def quantize_w4(w: torch.Tensor, group: int = W4_GROUP, clip_grid=None):
     return q.to(torch.uint8).view(n, k), best_scale, best_zero.to(torch.int16)
 
 
+def quantize_w4_sym(w: torch.Tensor, group: int = W4_GROUP):
+    """[N, K] -> (q uint8 0..15 standing for q - 8, scale bf16 [N, K/g]).
+
+    The symmetric int4 format with bf16 group scales that the benchmark's draft-head
+    configuration names (restated from that description: the reference module packs only its
+    asymmetric f16 scale + zero format, so there is no reference implementation to pin this
+    one to): per (row, group of 128) scale = bf16(amax / 7), q = clamp(round(w / scale), -8, 7)
+    + 8 by true division and round-half-even; an all-zero group keeps scale 0 and code 8."""
+    n, k = w.shape
+    assert k % group == 0
+    wf = w.float().view(n, k // group, group)
+    scale = (wf.abs().amax(-1) / 7.0).to(torch.bfloat16)
+    sf = scale.float().unsqueeze(-1)
+    r = torch.where(sf > 0, wf / torch.where(sf > 0, sf, torch.ones_like(sf)), torch.zeros_like(wf))
+    q = torch.round(r).clamp_(-8, 7) + 8
+    return q.to(torch.uint8).view(n, k), scale
+
+
+def w4_dequant_sym(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """(q - 8) * scale, fp32 [N, K]."""
+    n, k = q.shape
+    ng = scale.shape[1]
+    return ((q.float().view(n, ng, k // ng) - 8.0) * scale.float().unsqueeze(-1)).view(n, k)
+
+
 def w4_dequant(q: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:
     """fp32 ``(q - zero) * scale`` per (row, group) (draft_w4_lmhead.py:49-50, 281)."""
     n, k = q.shape

@@ -43,6 +43,8 @@ LMHEAD_PROTOS = {
     "hcq_stream_probe": (c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
     "b200_w4_lmhead": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_int, c_ll, c_vp,
                                c_ll, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
+    "b200_w4_lmhead_sym": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_int, c_ll, c_vp,
+                                   c_ll, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "r4d_gemm_w4a16_nt_m64": (None, [c_long] * 4 + [c_int] * 8 + [c_long]),
     "r4d_gemm_w4a16_nt_m64_last_error": (c_int, []),
     "r4d_gemm_w4a16_nt_m64_max_m": (c_int, []),

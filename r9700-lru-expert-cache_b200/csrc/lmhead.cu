@@ -54,10 +54,17 @@ constexpr int SMEM_CAP = 227 * 1024;
 constexpr int MAX_STAGES = 16;
 constexpr int FP8_KB_BYTES = 16 * 128;   // one strip x one 128-K block
 constexpr int W4_KB_BYTES = 16 * 64;
-constexpr int W4_SZ_BYTES = 16 * 4;
+constexpr int W4_SZ_BYTES = 16 * 4;     // per strip and 128-K block: 16 rows x (f16 scale | f16 -(1024+zero))
+constexpr int W4S_SZ_BYTES = 16 * 2;    // symmetric format: 16 rows x bf16 scale (zero fixed at 8)
 constexpr uint64_t WAIT_NS = 2000000000ull;   // 2 s bound on any pipeline wait
 
-enum Kind { FP8_QUANT = 0, FP8_PREQ = 1, W4_BF16 = 2, W4_F16 = 3 };
+enum Kind { FP8_QUANT = 0, FP8_PREQ = 1, W4_BF16 = 2, W4_F16 = 3, W4S_BF16 = 4, W4S_F16 = 5 };
+// W4 kinds: activation bf16 or f16; W4S = the symmetric format (codes q in 0..15 mean q - 8,
+// one bf16 scale per row and 128-K group).
+__host__ __device__ constexpr bool kind_w4(int k) { return k >= W4_BF16; }
+__host__ __device__ constexpr bool kind_w4s(int k) { return k >= W4S_BF16; }
+__host__ __device__ constexpr bool kind_bf16x(int k) { return k == W4_BF16 || k == W4S_BF16; }
+__host__ __device__ constexpr int kind_sz_bytes(int k) { return kind_w4s(k) ? W4S_SZ_BYTES : W4_SZ_BYTES; }
 
 __device__ int g_lmhead_err = 0;         // 1 = a pipeline wait timed out
 
@@ -173,7 +180,7 @@ __device__ void load_activation(const Params& p, char* sm, int rows_x, uint64_t*
     }
     return;
   }
-  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  constexpr bool IS_W4 = kind_w4(KIND);
   const int row_bytes = IS_W4 ? 2 * p.K : p.K;
   if (p.pdl) griddep_wait();
   if (ctid == 0) {
@@ -190,7 +197,7 @@ __device__ void load_activation(const Params& p, char* sm, int rows_x, uint64_t*
   if (!IS_W4)
     for (int i = ctid; i < rows_x * KB; i += NC * 32) xs[i] = (i / KB < p.M) ? p.xs_in[i] : 0.f;
   *ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(x_bar, 0, deadline));
-  if (KIND == W4_BF16) {
+  if (kind_bf16x(KIND)) {
     consumer_bar<NC>();                           // (every consumer warp reaches it)
     if (!*ok) return;
     for (int i = ctid; i < p.M * (p.K / 8); i += NC * 32) {
@@ -251,7 +258,7 @@ __device__ __forceinline__ void fp8_stage(const Params& p, const char* stage, co
   }
 }
 
-template <int NT8>
+template <int NT8, bool SYM>
 __device__ __forceinline__ void w4_stage(const Params& p, const char* stage, const char* xbase, int kb0,
                                          int nkb, float (&tot)[NT8][4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -261,12 +268,23 @@ __device__ __forceinline__ void w4_stage(const Params& p, const char* stage, con
     const char* tile = stage + j * W4_KB_BYTES;
     const uint4 A = *reinterpret_cast<const uint4*>(tile + (g * 4 + t) * 16);
     const uint4 B = *reinterpret_cast<const uint4*>(tile + ((8 + g) * 4 + t) * 16);
-    const uint32_t szA = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + g * 4);
-    const uint32_t szB = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
-    const float scA = __half2float(__ushort_as_half((unsigned short)(szA & 0xffffu)));
-    const float scB = __half2float(__ushort_as_half((unsigned short)(szB & 0xffffu)));
-    const uint32_t nzA = (szA >> 16) | (szA & 0xffff0000u);
-    const uint32_t nzB = (szB >> 16) | (szB & 0xffff0000u);
+    float scA, scB;
+    uint32_t nzA, nzB;
+    if constexpr (SYM) {
+      // bf16 scale; zero 8, so (nibble | 0x6400) + f16(-1032) = q - 8 exactly
+      const unsigned short sa = *reinterpret_cast<const unsigned short*>(szbase + j * W4S_SZ_BYTES + g * 2);
+      const unsigned short sb = *reinterpret_cast<const unsigned short*>(szbase + j * W4S_SZ_BYTES + (g + 8) * 2);
+      scA = __uint_as_float((uint32_t)sa << 16);
+      scB = __uint_as_float((uint32_t)sb << 16);
+      nzA = nzB = 0xE408E408u;
+    } else {
+      const uint32_t szA = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + g * 4);
+      const uint32_t szB = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
+      scA = __half2float(__ushort_as_half((unsigned short)(szA & 0xffffu)));
+      scB = __half2float(__ushort_as_half((unsigned short)(szB & 0xffffu)));
+      nzA = (szA >> 16) | (szA & 0xffff0000u);
+      nzB = (szB >> 16) | (szB & 0xffff0000u);
+    }
     const uint32_t wa[4] = {A.x, A.y, A.z, A.w}, wb[4] = {B.x, B.y, B.z, B.w};
     const int kb = kb0 + j;
     float acc[NT8][4];
@@ -327,8 +345,9 @@ __host__ __device__ constexpr int gemv_hdr(int nc) { return GEMV_HDR_RED + nc * 
 template <int KIND, int NT8, bool STATS, int NC>
 __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   extern __shared__ __align__(128) char sm[];
-  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  constexpr bool IS_W4 = kind_w4(KIND);
   constexpr int KB_BYTES = IS_W4 ? W4_KB_BYTES : FP8_KB_BYTES;
+  constexpr int SZB = kind_sz_bytes(KIND);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = p.K / 128;
   const int CH = (KB + p.kps - 1) / p.kps;
@@ -379,12 +398,12 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
         const long long blk = (long long)strip * KB + kb0;
         char* dst = ring + slot * p.stage_bytes;
         const uint32_t wbytes = nkb * KB_BYTES;
-        const uint32_t sbytes = IS_W4 ? nkb * W4_SZ_BYTES : 0;
+        const uint32_t sbytes = IS_W4 ? nkb * SZB : 0;
         b200::mbar_arrive_expect_tx(&full[slot], wbytes + sbytes);
         b200::bulk_g2s_stream(dst, p.w + blk * KB_BYTES, wbytes, &full[slot], pol);
         if (IS_W4)
           b200::bulk_g2s(dst + p.kps * W4_KB_BYTES,
-                         static_cast<const uint8_t*>(p.wscale) + blk * W4_SZ_BYTES, sbytes, &full[slot]);
+                         static_cast<const uint8_t*>(p.wscale) + blk * SZB, sbytes, &full[slot]);
         ++issued;
       }
       if (!ok) atomicExch(&g_lmhead_err, 1);
@@ -418,7 +437,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
         const char* stage = ring + slot * p.stage_bytes;
         const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
         if (IS_W4)
-          w4_stage<NT8>(p, stage, xbase, kb0, nkb, tot);
+          w4_stage<NT8, kind_w4s(KIND)>(p, stage, xbase, kb0, nkb, tot);
         else
           fp8_stage<NT8>(p, stage, xbase, xs, kb0, nkb, strip, tot);
         __syncwarp();
@@ -1320,14 +1339,14 @@ int allow_full_smem(const void* kern, bool (&done)[HOST_MAX_DEVICES]) {
 // previous round has already been issued, which holds when nstage >= (NC - 1) * CH + 1 (the
 // producer issues in order, and a consumer starting a strip has finished a stage at most
 // (NC - 1) * CH + 1 positions earlier). Plans below that bound are rejected.
-int plan(Params& p, bool is_w4, int nt8, int nc) {
+int plan(Params& p, bool is_w4, int nt8, int nc, int sz_bytes) {
   const int KB = p.K / 128;
   const int rows_x = 8 * nt8;
   p.xs_stride = (is_w4 ? 2 * p.K : p.K) + 64;
   p.xs_off = (gemv_hdr(nc) + 15) & ~15;
   p.x_off = (p.xs_off + MAXM * KB * 4 + 127) & ~127;
   const int fixed = p.x_off + rows_x * p.xs_stride;
-  const int per_kb = is_w4 ? (W4_KB_BYTES + W4_SZ_BYTES) : FP8_KB_BYTES;
+  const int per_kb = is_w4 ? (W4_KB_BYTES + sz_bytes) : FP8_KB_BYTES;
   // The largest stages (fewest, biggest bulk copies) that still give a safe ring.
   for (int kps = min(KB, 24); kps >= 1; --kps) {
     const int ch = (KB + kps - 1) / kps;
@@ -1366,9 +1385,9 @@ int launch_ex(void (*kern)(Exp...), dim3 grid, dim3 block, int smem, cudaStream_
 
 template <int KIND, int NT8, bool STATS>
 int launch_one(Params p, cudaStream_t stream) {
-  constexpr bool IS_W4 = (KIND == W4_BF16 || KIND == W4_F16);
+  constexpr bool IS_W4 = kind_w4(KIND);
   constexpr int NC = IS_W4 ? (NT8 == 1 ? NC_W4 : NC_W4_WIDE) : NC_FP8;
-  const int smem = plan(p, IS_W4, NT8, NC);
+  const int smem = plan(p, IS_W4, NT8, NC, IS_W4 ? kind_sz_bytes(KIND) : 0);
   if (smem < 0) return -8;
   auto kern = gemv_kernel<KIND, NT8, STATS, NC>;
   static bool smem_set[HOST_MAX_DEVICES] = {};
@@ -1701,7 +1720,7 @@ int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream)
 // are padding (written to y, excluded from the row statistics). Same outputs as
 // b200_fp8_lmhead. Returns 0, -1 bad M, -2 N_pad % 16, -3 K % 128, -8 smem, -9 workspace,
 // -10 alignment, -11 bad dtype.
-int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+static int w4_lmhead_impl(bool sym, const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
                    int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
                    float* row_max, long long* row_arg, float* row_lse, void* workspace,
                    long long workspace_bytes, cudaStream_t stream) {
@@ -1722,7 +1741,26 @@ int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, con
   p.row_max = row_max; p.row_arg = row_arg; p.row_lse = row_lse;
   p.ws = static_cast<char*>(workspace);
   p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
+  if (sym) return x_dtype == 0 ? run_chunks<W4S_BF16>(p, 2, stream) : run_chunks<W4S_F16>(p, 2, stream);
   return x_dtype == 0 ? run_chunks<W4_BF16>(p, 2, stream) : run_chunks<W4_F16>(p, 2, stream);
+}
+
+int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+                   int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                   float* row_max, long long* row_arg, float* row_lse, void* workspace,
+                   long long workspace_bytes, cudaStream_t stream) {
+  return w4_lmhead_impl(false, x, x_dtype, M, K, wq, wsz, N_pad, n_valid, vocab_offset, y, ldy, row_max,
+                        row_arg, row_lse, workspace, workspace_bytes, stream);
+}
+
+// The same head for the symmetric format: `wscale` holds bf16 scales [N_pad/16, K/128, 16]
+// (strip, 128-K group, row in strip); a code q in 0..15 stands for (q - 8) * scale.
+int b200_w4_lmhead_sym(const void* x, int x_dtype, int M, int K, const void* wq, const void* wscale,
+                       int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                       float* row_max, long long* row_arg, float* row_lse, void* workspace,
+                       long long workspace_bytes, cudaStream_t stream) {
+  return w4_lmhead_impl(true, x, x_dtype, M, K, wq, wscale, N_pad, n_valid, vocab_offset, y, ldy, row_max,
+                        row_arg, row_lse, workspace, workspace_bytes, stream);
 }
 
 static int g_w4_last_rc = 0;

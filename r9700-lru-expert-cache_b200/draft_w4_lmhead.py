@@ -45,16 +45,18 @@ _CLIP_GRID = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7, 0.65, 0.6)
 
 @dataclass(frozen=True)
 class PackedW4:
-    """Everything ``gemm_w4a16`` needs; hold this on the layer."""
+    """Everything ``gemm_w4a16`` needs; hold this on the layer. ``sym`` marks the symmetric
+    format (pack_w4a16_sym): ``wsz`` then holds bf16 scales and every zero is 8."""
     wq: torch.Tensor     # uint8  [N_pad/16, K/128, 1024]  (= N_pad*K/2 bytes)
-    wsz: torch.Tensor    # int32  [N_pad/16, K/128, 16]
+    wsz: torch.Tensor    # int32  [N_pad/16, K/128, 16]  (bf16 [N_pad/16, K/128, 16] when sym)
     n: int
     n_pad: int
     k: int
+    sym: bool = False
 
     @property
     def nbytes(self) -> int:
-        return self.wq.numel() + self.wsz.numel() * 4
+        return self.wq.numel() + self.wsz.numel() * self.wsz.element_size()
 
 
 @functools.lru_cache(maxsize=1)
@@ -179,6 +181,47 @@ def pack_w4a16(weight: torch.Tensor, group: int = 0, chunk_tiles: int = 512,
     return PackedW4(wq=wq_out, wsz=sz_out, n=n, n_pad=n_pad, k=k)
 
 
+def quantize_w4_sym(w: torch.Tensor, group: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """[N, K] -> (q uint8 in 0..15 meaning q - 8, scale bf16 [N, K/group]): symmetric int4 per
+    (row, group) with a bf16 scale = amax / 7 (the benchmark's draft-head format); codes by true
+    division and round-half-even, clamped to [-8, 7]; an all-zero group keeps scale 0."""
+    group = group or GROUP
+    n, k = w.shape
+    assert k % group == 0, f"K={k} must be a multiple of the group {group}"
+    wf = w.float().view(n, k // group, group)
+    scale = (wf.abs().amax(-1) / 7.0).to(torch.bfloat16)
+    sf = scale.float().unsqueeze(-1)
+    ratio = torch.where(sf > 0, wf / torch.where(sf > 0, sf, torch.ones_like(sf)), torch.zeros_like(wf))
+    q = torch.round(ratio).clamp_(-8, 7) + 8
+    return q.to(torch.uint8).view(n, k), scale
+
+
+def pack_w4a16_sym(weight: torch.Tensor, group: int = 0, chunk_tiles: int = 512) -> PackedW4:
+    """[N, K] lm_head weight -> PackedW4 in the symmetric format (bf16 group scales, zero 8):
+    the same code layout as pack_w4a16, scales as bf16 [N_pad/16, K/128, 16]."""
+    assert weight.dim() == 2, f"expected [N, K], got {tuple(weight.shape)}"
+    _fns()
+    group = group or GROUP
+    n, k = weight.shape
+    if k % 128 or k % group or group != 128:
+        raise ValueError(f"draft_w4_lmhead: K={k} must be a multiple of 128 (group 128)")
+    n_pad = (n + 15) // 16 * 16
+    dev = weight.device
+    wq_out = torch.empty((n_pad // 16, k // 128, 1024), dtype=torch.uint8, device=dev)
+    sc_out = torch.empty((n_pad // 16, k // group, 16), dtype=torch.bfloat16, device=dev)
+    rows = chunk_tiles * 16
+    for r0 in range(0, n_pad, rows):
+        r1 = min(r0 + rows, n_pad)
+        w = weight[r0:min(r1, n)]
+        if w.shape[0] < r1 - r0:
+            w = torch.cat([w, w.new_zeros(r1 - r0 - w.shape[0], k)], 0)
+        q, scale = quantize_w4_sym(w, group)
+        wq_out[r0 // 16:r1 // 16] = _pack_codes(q)
+        sc_out[r0 // 16:r1 // 16] = scale.view((r1 - r0) // 16, 16, k // group).permute(0, 2, 1)
+        del q, scale, w
+    return PackedW4(wq=wq_out, wsz=sc_out, n=n, n_pad=n_pad, k=k, sym=True)
+
+
 def unpack_w4(packed: PackedW4, dtype: torch.dtype = torch.bfloat16,
               rows: slice | None = None) -> torch.Tensor:
     """Dequantize back to [N_pad, K] -- the inverse of pack_w4a16, for the numeric reference
@@ -190,8 +233,12 @@ def unpack_w4(packed: PackedW4, dtype: torch.dtype = torch.bfloat16,
     q = _unpack_codes(packed.wq, packed.n_pad, k, t0, t1).float()
     ng = packed.wsz.shape[1]
     sz = packed.wsz[t0:t1].permute(0, 2, 1).reshape((t1 - t0) * 16, ng)
-    scale = (sz & 0xFFFF).to(torch.int16).view(torch.float16).float()
-    zero = -(sz >> 16).to(torch.int16).view(torch.float16).float() - 1024.0
+    if packed.sym:
+        scale = sz.float()
+        zero = torch.full_like(scale, 8.0)
+    else:
+        scale = (sz & 0xFFFF).to(torch.int16).view(torch.float16).float()
+        zero = -(sz >> 16).to(torch.int16).view(torch.float16).float() - 1024.0
     w = (q.view((t1 - t0) * 16, ng, k // ng) - zero.unsqueeze(-1)) * scale.unsqueeze(-1)
     w = w.view((t1 - t0) * 16, k).to(dtype)
     if rows is not None:
@@ -253,6 +300,9 @@ def _run(x: torch.Tensor, wq: torch.Tensor, wsz: torch.Tensor, n: int, k: int,
     fn = _fns()
     if fn is None:
         raise RuntimeError("draft_w4_lmhead: the B200 kernel is unavailable on this machine")
+    sym = wsz.dtype == torch.bfloat16                       # the symmetric format's scales
+    if sym:
+        fn = _lib.lmhead().b200_w4_lmhead_sym
     _lib.require_cuda("draft_w4_lmhead", x, wq, wsz)
     m = x.shape[0]
     n_pad = wq.shape[0] * 16
@@ -271,7 +321,7 @@ def _run(x: torch.Tensor, wq: torch.Tensor, wsz: torch.Tensor, n: int, k: int,
     rc = fn(_lib.ptr(x), 0 if x.dtype == torch.bfloat16 else 1, m, k, _lib.ptr(wq), _lib.ptr(wsz),
             n_pad, n, int(vocab_offset), _lib.ptr(y), y.stride(0), _lib.ptr(mx), _lib.ptr(arg),
             _lib.ptr(lse), _lib.ptr(wsp), 0 if wsp is None else wsp.numel(), _lib.stream_ptr())
-    _lib.check(rc, "b200_w4_lmhead")
+    _lib.check(rc, "b200_w4_lmhead_sym" if sym else "b200_w4_lmhead")
     return y, mx, arg, lse
 
 

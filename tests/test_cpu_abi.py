@@ -174,6 +174,27 @@ def test_product_w4_packer_reproduces_reference(n, k):
         assert up.double().sum().item() == pytest.approx(s[0], abs=1e-9)
 
 
+@pytest.mark.parametrize("n,k", [(48, 256), (200, 384)])
+def test_product_w4_sym_packer_matches_oracle(n, k):
+    """The symmetric bf16-scale format (no reference implementation exists): the package's
+    quantizer equals the oracle's restatement bit for bit (all-zero and single-spike groups
+    included), and unpack(pack) equals the oracle's dequantization exactly."""
+    W = P.draft_w4_lmhead
+    g = torch.Generator().manual_seed(n * k)
+    w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+    w[1, :128] = 0
+    w[2, 128:256] = 0
+    w[2, 130] = 0.3
+    q1, s1 = W.quantize_w4_sym(w)
+    q2, s2 = Q.quantize_w4_sym(w)
+    assert torch.equal(q1, q2) and torch.equal(s1.view(torch.int16), s2.view(torch.int16))
+    assert q1.max().item() <= 15 and s1[1, 0].item() == 0 and q1[1, :128].eq(8).all()
+    p = W.pack_w4a16_sym(w)
+    assert p.sym and p.wsz.dtype == torch.bfloat16 and p.nbytes == p.n_pad * k // 2 + p.n_pad * k // 128 * 2
+    assert torch.equal(W._unpack_codes(p.wq, p.n_pad, k)[:n], q2)
+    assert torch.equal(W.unpack_w4(p, torch.float32)[:n], Q.w4_dequant_sym(q2, s2))
+
+
 def test_product_fp8_packer_reproduces_reference():
     g = golden("fp8_pack_reference.npz")
     F8 = P.fp8_target_lmhead

@@ -210,6 +210,33 @@ def test_w4_padding_and_top(cuda):
     assert (lse.cpu() - rlse.cpu()).abs().max().item() < 1e-3
 
 
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_w4_sym_format(cuda, M):
+    """Symmetric int4 with bf16 group scales (b200_w4_lmhead_sym): logits against
+    F.linear(f16(x), dequant) within the reference's rel-Frobenius 5e-3, the opaque op and the
+    fused top-k path agree, argmax exact where the top-2 gap allows, padding never wins."""
+    n, k = 1000, 2560
+    g = torch.Generator(device=cuda).manual_seed(M)
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.02).bfloat16()
+    w[996] = 0.4
+    p = W4.pack_w4a16_sym(w)
+    x = torch.randn(M, k, device=cuda, generator=g).bfloat16()
+    x[0] = x[0].abs()
+    y = W4.gemm_w4a16(x, p)
+    wref = W4.unpack_w4(p, torch.float32)[:n]
+    r = F.linear(x.float().half().float(), wref)
+    assert y.shape == (M, n) and _rel(y, r) < 5e-3
+    logits, mx, arg, lse = W4.gemm_w4a16_top(x, p, vocab_offset=7)
+    assert torch.equal(logits, y)
+    rmx, rarg, rlse = Q.row_stats(r)
+    gap = Q.top2_gap(r)
+    for m in range(M):
+        if gap[m] > 1e-3:
+            assert int(arg[m]) == int(rarg[m]) + 7
+    assert (lse.cpu() - rlse.cpu()).abs().max().item() < 1e-3
+    assert P._lib.lmhead().b200_lmhead_error(1) == 0
+
+
 def test_w4_reference_c_abi_f16(cuda):
     """r4d_gemm_w4a16_nt_m64 with an f16 activation (the reference's call, draft_w4_lmhead.py:363-369)."""
     n, k, M = 512, 2560, 5
@@ -225,13 +252,13 @@ def test_w4_reference_c_abi_f16(cuda):
     assert torch.equal(c, W4.gemm_w4a16(x, p))
 
 
-@pytest.mark.parametrize("M", [4, 16])
-def test_w4_baseline_shape(cuda, M):
+@pytest.mark.parametrize("M,sym", [(4, False), (16, False), (4, True)])
+def test_w4_baseline_shape(cuda, M, sym):
     """Full draft head: x [M, 2560] ~N(0,1), W ~N(0,0.02) [151936, 2560]; M=16 takes the wider
     activation region (fewer ring stages); the device error word must stay clear."""
     n, k = 151936, 2560
     w = (torch.randn(n, k, device=cuda, generator=torch.Generator(device=cuda).manual_seed(0)) * 0.02).bfloat16()
-    p = W4.pack_w4a16(w)
+    p = W4.pack_w4a16_sym(w) if sym else W4.pack_w4a16(w)
     del w
     x = torch.randn(M, k, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1)).bfloat16()
     logits, mx, arg, lse = W4.gemm_w4a16_top(x, p)
