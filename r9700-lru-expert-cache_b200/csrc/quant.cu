@@ -10,9 +10,10 @@
 //   following per_token_group_quant_fp8: scale = max(amax, 1e-10) * fp32(1/448).
 //
 // B200 mapping: one warp per row (4 rows per 128-thread CTA), 16-byte loads of 8 elements
-// when the row is 16-byte aligned, warp-shuffle amax. The activation is recomputed in the
-// second pass instead of being held in registers, so any d up to the reference's 8192
-// bound runs with the same code and the recomputation is bit-identical by construction.
+// when the row is 16-byte aligned, warp-shuffle amax. Rows up to 1024 wide keep the
+// activation in registers between the amax and the quantization (one pass); wider or
+// unaligned rows recompute it in a second pass, bit-identical by construction, so any d up
+// to the reference's 8192 bound runs.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -155,6 +156,53 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
   }
 }
 
+// Per-row scale, rows of at most 32 * 8 * RC elements (16-byte aligned): one pass. Each lane
+// keeps its RC chunks of the activation in registers between the amax and the quantization,
+// so every element costs one expf and two divisions instead of twice that; the values are
+// those of silu_mul_quant_kernel bit for bit (same expressions, same order).
+template <typename T, int RC>
+__global__ void __launch_bounds__(32 * ROWS_PER_CTA)
+    silu_mul_quant_reg_kernel(const T* __restrict__ x, long long stride_x, int rows, int d,
+                              uint8_t* __restrict__ q, float* __restrict__ scale, T* __restrict__ act) {
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const T* xg = x + (long long)row * stride_x;
+  const T* xu = xg + d;
+  const int nchunk = d / 8;
+  float af[RC][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < RC; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nchunk) {
+      T g[8], u[8], a[8];
+      load8<T, true>(xg + 8 * c, 8, g);
+      load8<T, true>(xu + 8 * c, 8, u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        af[j][i] = silu_mul_elem<T>(g[i], u[i], &a[i]);
+        amax = fmaxf(amax, fabsf(af[j][i]));
+      }
+      if (act != nullptr)
+        *reinterpret_cast<uint4*>(act + (long long)row * d + 8 * c) = *reinterpret_cast<const uint4*>(a);
+    }
+  }
+  amax = b200::warp_max(amax);
+  const float sc = fmaxf(amax / kFp8Max, kMinScale);
+  if (lane == 0) scale[row] = sc;
+#pragma unroll
+  for (int j = 0; j < RC; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nchunk) {
+      uint8_t b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(af[j][i] / sc, -kFp8Max), kFp8Max));
+      *reinterpret_cast<uint2*>(q + (long long)row * d + 8 * c) = *reinterpret_cast<const uint2*>(b);
+    }
+  }
+}
+
 // Per-token group quant of a [M, K] activation: half a warp per 128-wide group.
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -203,7 +251,14 @@ int launch_silu(const void* x, long long stride_x, int rows, int d, void* q, flo
   uint8_t* qp = static_cast<uint8_t*>(q);
   T* ap = static_cast<T*>(act);
   if (group == 0) {
-    if (vec)
+    const int nchunk = d / 8;
+    if (vec && nchunk <= 32)
+      silu_mul_quant_reg_kernel<T, 1><<<grid, block, 0, stream>>>(xp, stride_x, rows, d, qp, scale, ap);
+    else if (vec && nchunk <= 64)
+      silu_mul_quant_reg_kernel<T, 2><<<grid, block, 0, stream>>>(xp, stride_x, rows, d, qp, scale, ap);
+    else if (vec && nchunk <= 128)
+      silu_mul_quant_reg_kernel<T, 4><<<grid, block, 0, stream>>>(xp, stride_x, rows, d, qp, scale, ap);
+    else if (vec)
       silu_mul_quant_kernel<T, true, 0><<<grid, block, 0, stream>>>(xp, stride_x, rows, d, qp, scale, ap);
     else
       silu_mul_quant_kernel<T, false, 0><<<grid, block, 0, stream>>>(xp, stride_x, rows, d, qp, scale, ap);

@@ -26,6 +26,8 @@ def _eq(a, b):
 
 
 GRID = [(r, d, s) for r in (1, 10, 50, 80, 2048) for d in (320, 640) for s in (1.0, 1e-3, 60.0)]
+# row widths at the one-pass kernel's register bounds (256 / 512 / 1024) and past them (two-pass)
+GRID += [(33, d, 1.0) for d in (8, 256, 264, 512, 1024, 1032, 4096, 8192)]
 
 
 @pytest.mark.parametrize("rows,d,sc", GRID)
