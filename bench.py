@@ -141,8 +141,8 @@ def cpu_baseline_fp8(sample_rows: int = 16384, reps: int = 3) -> dict:
 def cpu_baseline_ops() -> dict:
     """The reference's CPU forms of the other ops on this box's host cores, bounded samples:
     W4 head = dequantize (unpack) + fp32 matmul (the reference's M > 64 fallback form) on a
-    vocabulary sample; LRU = the numpy reference model's manage step per layer; SiLU-quant =
-    the torch eager restatement at the decode shape."""
+    vocabulary sample; LRU = the numpy reference model's manage step per layer; SiLU-quant and
+    the shared-expert gate = the torch eager restatements at the decode shapes."""
     from oracle import lru_oracle as LO
     from oracle import quant_oracle as Q
     res = {}
@@ -172,6 +172,13 @@ def cpu_baseline_ops() -> dict:
     for _ in range(20):
         Q.silu_mul_quant(xs)
     res["silu_mul_quant_T8_d512_us"] = (time.perf_counter() - t0) / 20 * 1e6
+    from oracle import moe_tail_oracle as GO
+    out, g = torch.randn(20, K_HID).bfloat16(), torch.randn(20, 1).bfloat16()
+    GO.sigmoid_gate_mul(g, out)
+    t0 = time.perf_counter()
+    for _ in range(50):
+        GO.sigmoid_gate_mul(g, out)
+    res["gate_mul_T20_us"] = (time.perf_counter() - t0) / 50 * 1e6
     res["cores"] = torch.get_num_threads()
     return res
 
@@ -345,6 +352,64 @@ def ops_bench(P, dev) -> dict:
     us = time_graph(silu_big, 2 * len(bufs), dev)
     nb = T * 2 * d * 2 + T * d + T * 4
     res[f"silu_mul_quant_T{T}_d{d}"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
+    del bufs
+    # shared-expert gate at the decode shape [20, 2560], beside the stock two-kernel forms
+    FG = P.fused_gate_mul
+    out = torch.randn(20, K_HID, device=dev, dtype=torch.bfloat16)
+    g = torch.randn(20, 1, device=dev, dtype=torch.bfloat16)
+    xg = torch.randn(20, K_HID, device=dev, dtype=torch.bfloat16)
+    wg = torch.randn(1, K_HID, device=dev, dtype=torch.bfloat16) * 0.02
+    res["gate_mul_T20"] = {"us_per_call": time_graph(lambda: FG.sigmoid_gate_mul(g, out), 200, dev),
+                           "stock_us_per_call": time_graph(lambda: torch.sigmoid(g) * out, 200, dev)}
+    res["gemv_gate_mul_T20"] = {
+        "us_per_call": time_graph(lambda: FG.gemv_sigmoid_gate_mul(xg, wg, out), 200, dev),
+        "stock_us_per_call": time_graph(
+            lambda: torch.sigmoid(torch.nn.functional.linear(xg, wg)) * out, 200, dev)}
+    # and at a prefill-sized [16384, 2560] through a pool larger than L2 (HBM-bound)
+    T = 16384
+    outs = [torch.randn(T, K_HID, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    gs = [torch.randn(T, 1, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    it = {"i": 0}
+
+    def gate_big():
+        j = it["i"] % len(outs)
+        FG.sigmoid_gate_mul(gs[j], outs[j])
+        it["i"] += 1
+    us = time_graph(gate_big, 2 * len(outs), dev)
+    nb = 2 * T * K_HID * 2 + T * 2
+    res[f"gate_mul_T{T}"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
+    del outs, gs
+    # per-token FP8 quant of the MoE hidden states (fp8_quant_shared) at decode and prefill
+    HQ = P.fp8_hidden_quant
+    xh = torch.randn(20, K_HID, device=dev, dtype=torch.bfloat16)
+    res["hidden_quant_T20"] = {
+        "us_per_call": time_graph(lambda: HQ.scaled_fp8_quant(xh, use_per_token_if_dynamic=True), 200, dev)}
+    xs_big = [torch.randn(T, K_HID, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    it = {"i": 0}
+
+    def hq_big():
+        HQ.scaled_fp8_quant(xs_big[it["i"] % len(xs_big)], use_per_token_if_dynamic=True)
+        it["i"] += 1
+    us = time_graph(hq_big, 2 * len(xs_big), dev)
+    nb = T * K_HID * 3 + T * 4
+    res[f"hidden_quant_T{T}"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
+    del xs_big
+    # moe_sum over top_k = 10 routed rows per token: decode (M = 20) and M = 2048 over a pool
+    MO = P.moe_ops
+    ic3 = torch.randn(20, TOPK, K_HID, device=dev, dtype=torch.bfloat16)
+    osum = torch.empty(20, K_HID, device=dev, dtype=torch.bfloat16)
+    res["moe_sum_T20_k10"] = {"us_per_call": time_graph(lambda: MO.moe_sum(ic3, osum), 200, dev)}
+    Tm = 2048
+    ins = [torch.randn(Tm, TOPK, K_HID, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    osum = torch.empty(Tm, K_HID, device=dev, dtype=torch.bfloat16)
+    it = {"i": 0}
+
+    def ms_big():
+        MO.moe_sum(ins[it["i"] % len(ins)], osum)
+        it["i"] += 1
+    us = time_graph(ms_big, 2 * len(ins), dev)
+    nb = Tm * TOPK * K_HID * 2 + Tm * K_HID * 2
+    res[f"moe_sum_T{Tm}_k10"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
     return res
 
 

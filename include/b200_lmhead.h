@@ -36,6 +36,14 @@ int b200_silu_mul_quant(const void* x, int rows, int d, long long stride_x, int 
 int b200_per_token_group_quant_fp8(const void* x, int M, int K, long long stride_x, int dtype,
                                    int group, void* q, float* s, cudaStream_t stream);
 
+/* scaled_fp8_quant(x, use_per_token_if_dynamic=True) (vLLM), the MoE hidden-state quant behind
+ * fp8_quant_shared (patches/model_executor/kernels/linear/mxfp4/r4dhip.py.diff L19-34):
+ * amax = min(max |x_row|, *scale_ub if given), scale = max(amax/448, 1/(448*512)),
+ * q = e4m3(clamp(x / scale)). x [rows, K] with row stride stride_x; q [rows, K] contiguous;
+ * scale fp32 [rows]. -1 negative sizes or stride_x < K; -2 bad dtype. */
+int b200_per_token_quant_fp8(const void* x, int rows, int K, long long stride_x, int dtype,
+                             const float* scale_ub, void* q, float* scale, cudaStream_t stream);
+
 /* Bytes of the caller-owned scratch the fused lm_head entries use (activation tiles and rows,
  * per-CTA row statistics, partial accumulators). It needs no initialisation; calls that share
  * it must not overlap on the GPU. */

@@ -6,6 +6,9 @@ called on CUDA tensors (in the GPU tests) it is the "torch-GPU eager restatement
 
 Sources followed (davetha/r9700-lru-expert-cache):
 * ``silu_mul_quant``  -- kernels/fused_silu_mul_quant.py:43-57 (rounding spelled out :9-14)
+* ``per_token_quant_fp8`` -- vLLM ``scaled_fp8_quant(use_per_token_if_dynamic=True)`` as called by
+  ``fp8_quant_shared`` (patches/model_executor/kernels/linear/mxfp4/r4dhip.py.diff L19-34);
+  the same scale and division as fused_silu_mul_quant.py:51-57 without the SiLU
 * ``group_quant_fp8`` -- vLLM ``per_token_group_quant_fp8`` as called at
   kernels/fp8_target_lmhead.py:73; vLLM 0.22 fp8_utils.py ``_per_token_group_quant_fp8``
   (amax floored at eps, scale = amax * fp32(1/448), q = e4m3(clamp(x / scale)))
@@ -75,6 +78,19 @@ def group_quant_fp8(x: torch.Tensor, group: int = BLK, eps: float = GROUP_EPS):
     s = amax * torch.full_like(amax, 1.0 / FP8_MAX)          # amax * fp32(1/448)
     q = (xf / s.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(FP8).reshape(M, K)
     return q, s.contiguous()
+
+
+def per_token_quant_fp8(x: torch.Tensor, scale_ub: torch.Tensor | None = None):
+    """vLLM ``scaled_fp8_quant(x, use_per_token_if_dynamic=True)`` as fp8_quant_shared calls
+    it (r4dhip.py.diff L19-34): row amax (capped by ``scale_ub``), scale = max(amax / 448,
+    1/(448*512)) with a true division, q = e4m3(clamp(x / scale)). -> (q [M, K], scale [M, 1])."""
+    xf = x.float()
+    amax = xf.abs().amax(dim=1, keepdim=True) if xf.shape[1] else xf.new_zeros(xf.shape[0], 1)
+    if scale_ub is not None:
+        amax = torch.minimum(amax, scale_ub.float().reshape(1, 1).to(amax.device))
+    scale = torch.clamp_min(amax / torch.full_like(amax, FP8_MAX), MIN_SCALE)
+    q = (xf / scale).clamp(-FP8_MAX, FP8_MAX).to(FP8)
+    return q, scale
 
 
 def silu_mul_quant_group(x: torch.Tensor, group: int = BLK, write_act: bool = False):

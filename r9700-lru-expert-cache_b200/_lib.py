@@ -26,6 +26,7 @@ RLU_PROTOS = {
 LMHEAD_PROTOS = {
     "b200_silu_mul_quant": (c_int, [c_vp, c_int, c_int, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_vp]),
     "b200_per_token_group_quant_fp8": (c_int, [c_vp, c_int, c_int, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
+    "b200_per_token_quant_fp8": (c_int, [c_vp, c_int, c_int, c_ll, c_int, c_vp, c_vp, c_vp, c_vp]),
     "b200_lmhead_workspace_bytes": (c_ll, []),
     "b200_lmhead_error": (c_int, [c_int]),
     "b200_fp8_lmhead": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_ll, c_vp, c_ll,
@@ -45,6 +46,10 @@ LMHEAD_PROTOS = {
                                c_ll, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "b200_w4_lmhead_sym": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_int, c_ll, c_vp,
                                    c_ll, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
+    "b200_sigmoid_gate_mul": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_vp]),
+    "b200_gemv_sigmoid_gate_mul": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll,
+                                           c_int, c_vp]),
+    "b200_moe_sum": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_ll, c_int, c_vp]),
     "r4d_gemm_w4a16_nt_m64": (None, [c_long] * 4 + [c_int] * 8 + [c_long]),
     "r4d_gemm_w4a16_nt_m64_last_error": (c_int, []),
     "r4d_gemm_w4a16_nt_m64_max_m": (c_int, []),

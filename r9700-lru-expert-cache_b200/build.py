@@ -1,8 +1,9 @@
 """Build the two C-ABI shared libraries of this package, in-tree, for sm_100a.
 
 * ``librlu.so``       -- csrc/lru.cu: r4d_lru_manage / r4d_lru_fused / r4d_lru_gather.
-* ``libb200lmhead.so`` -- csrc/quant.cu + csrc/lmhead.cu: SiLU-mul FP8 quant, per-token group
-  quant, FP8 and W4 lm_head GEMVs, the stream control.
+* ``libb200lmhead.so`` -- csrc/quant.cu + csrc/lmhead.cu + csrc/gate.cu + csrc/moe_sum.cu:
+  SiLU-mul FP8 quant, per-token (group) FP8 quant, FP8 and W4 lm_head GEMVs, the stream
+  control, the shared-expert gate and the routed experts' sum.
 
 No fast math: the SiLU-quant parity needs IEEE division and the accurate expf.
 Usage: ``python build.py [--force]`` (also called by ``__graft_entry__.build()``).
@@ -22,7 +23,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
 
 LIBS = {
     "librlu.so": ["lru.cu"],
-    "libb200lmhead.so": ["quant.cu", "lmhead.cu"],
+    "libb200lmhead.so": ["quant.cu", "lmhead.cu", "gate.cu", "moe_sum.cu"],
 }
 
 

@@ -203,6 +203,106 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
   }
 }
 
+// Per-token dynamic FP8 quant of a [rows, K] activation (vLLM scaled_fp8_quant with
+// use_per_token_if_dynamic=True): amax = max |x| over the row, clipped to *scale_ub when
+// given, scale = max(amax / 448, 1 / (448 * 512)), q = e4m3(clamp(x / scale, +-448)) with a
+// true division. One warp per row. RC > 0: the row (16-byte aligned, K % 8 == 0, at most
+// 256 * RC elements) stays in registers as raw 16-byte chunks between the amax and the
+// quantization, so HBM is read once; RC == 0: two passes over the row (the second is served
+// by L1 / L2), for wide or unaligned rows.
+template <typename T, int RC, bool VEC>
+__global__ void __launch_bounds__(32 * ROWS_PER_CTA)
+    token_quant_kernel(const T* __restrict__ x, long long stride_x, int rows, int K,
+                       const float* __restrict__ scale_ub, uint8_t* __restrict__ q,
+                       float* __restrict__ scale) {
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const T* xr = x + (long long)row * stride_x;
+  uint8_t* qr = q + (long long)row * K;
+  const int nchunk = (K + 7) / 8;
+  float amax = 0.f;
+  uint4 keep[RC > 0 ? RC : 1];
+  if constexpr (RC > 0) {
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nchunk) keep[j] = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+    }
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+      if (lane + 32 * j < nchunk) {
+        const T* v = reinterpret_cast<const T*>(&keep[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(to_f(v[i])));
+      }
+    }
+  } else {
+    for (int c = lane; c < nchunk; c += 32) {
+      T v[8];
+      load8<T, VEC>(xr + 8 * c, min(8, K - 8 * c), v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(to_f(v[i])));
+    }
+  }
+  amax = b200::warp_max(amax);
+  if (scale_ub != nullptr) amax = fminf(amax, *scale_ub);
+  const float sc = fmaxf(amax / kFp8Max, kMinScale);
+  if (lane == 0) scale[row] = sc;
+  if constexpr (RC > 0) {
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nchunk) {
+        const T* v = reinterpret_cast<const T*>(&keep[j]);
+        uint8_t b[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(to_f(v[i]) / sc, -kFp8Max), kFp8Max));
+        *reinterpret_cast<uint2*>(qr + 8 * c) = *reinterpret_cast<const uint2*>(b);
+      }
+    }
+  } else {
+    for (int c = lane; c < nchunk; c += 32) {
+      const int nv = min(8, K - 8 * c);
+      T v[8];
+      load8<T, VEC>(xr + 8 * c, nv, v);
+      uint8_t b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(to_f(v[i]) / sc, -kFp8Max), kFp8Max));
+      if (VEC) {
+        *reinterpret_cast<uint2*>(qr + 8 * c) = *reinterpret_cast<const uint2*>(b);
+      } else {
+        for (int i = 0; i < nv; ++i) qr[8 * c + i] = b[i];
+      }
+    }
+  }
+}
+
+template <typename T>
+int launch_token_quant(const void* x, long long stride_x, int rows, int K, const float* ub,
+                       void* q, float* scale, cudaStream_t stream) {
+  const bool vec = (K % 8 == 0) && (stride_x % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
+  const dim3 grid((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA), block(32 * ROWS_PER_CTA);
+  const T* xp = static_cast<const T*>(x);
+  uint8_t* qp = static_cast<uint8_t*>(q);
+  const int nchunk = K / 8;
+  if (vec && nchunk <= 32 * 4)
+    token_quant_kernel<T, 4, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (vec && nchunk <= 32 * 8)
+    token_quant_kernel<T, 8, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (vec && nchunk <= 32 * 12)
+    token_quant_kernel<T, 12, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (vec && nchunk <= 32 * 16)
+    token_quant_kernel<T, 16, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (vec)
+    token_quant_kernel<T, 0, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else
+    token_quant_kernel<T, 0, false><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  return (int)cudaGetLastError();
+}
+
 // Per-token group quant of a [M, K] activation: half a warp per 128-wide group.
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -287,6 +387,21 @@ int b200_silu_mul_quant(const void* x, int rows, int d, long long stride_x, int 
   if (dtype == 0) return launch_silu<__nv_bfloat16>(x, stride_x, rows, d, q, scale, act, group, stream);
   if (dtype == 1) return launch_silu<__half>(x, stride_x, rows, d, q, scale, act, group, stream);
   return -2;
+}
+
+// scaled_fp8_quant(x, use_per_token_if_dynamic=True) of a [rows, K] activation with row
+// stride `stride_x` (the MoE hidden-state quant behind fp8_quant_shared,
+// patches/model_executor/kernels/linear/mxfp4/r4dhip.py.diff L19-34): q e4m3 [rows, K]
+// contiguous, scale fp32 [rows]; scale_ub: optional device fp32 scalar that caps the row
+// amax (nullable). dtype 0 = bf16, 1 = f16. Returns 0, -1 for negative sizes or
+// stride_x < K, -2 for a bad dtype, else a CUDA error code.
+int b200_per_token_quant_fp8(const void* x, int rows, int K, long long stride_x, int dtype,
+                             const float* scale_ub, void* q, float* scale, cudaStream_t stream) {
+  if (rows < 0 || K < 0 || (rows > 1 && stride_x < K)) return -1;
+  if (dtype != 0 && dtype != 1) return -2;
+  if (rows == 0) return 0;
+  if (dtype == 0) return launch_token_quant<__nv_bfloat16>(x, stride_x, rows, K, scale_ub, q, scale, stream);
+  return launch_token_quant<__half>(x, stride_x, rows, K, scale_ub, q, scale, stream);
 }
 
 // per_token_group_quant_fp8(x, group) (called at kernels/fp8_target_lmhead.py:73) for a

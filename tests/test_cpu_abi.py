@@ -28,9 +28,10 @@ def _declared(header: str) -> list[str]:
     return re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\([^;{]*\)\s*;", src)
 
 
-@pytest.mark.parametrize("header,lib", [("r4d_lru.h", "librlu.so"), ("b200_lmhead.h", "libb200lmhead.so")])
-def test_every_declared_symbol_is_exported(header, lib):
-    names = _declared(header)
+@pytest.mark.parametrize("headers,lib", [(["r4d_lru.h"], "librlu.so"),
+                                         (["b200_lmhead.h", "b200_moe_tail.h"], "libb200lmhead.so")])
+def test_every_declared_symbol_is_exported(headers, lib):
+    names = [n for h in headers for n in _declared(h)]
     assert len(names) >= 3
     cdll = L.load(lib)
     for n in names:

@@ -148,3 +148,70 @@ def test_group_quant_matches_vllm_triton(cuda):
     nq = int((q.view(torch.uint8) != xq.view(torch.uint8)).sum())
     print(f"vs vLLM Triton group quant: scales {ns}/{s.numel()} differ, bytes {nq}/{q.numel()} differ")
     assert ns == 0 and nq <= q.numel() // 100
+
+
+# ---- per-token hidden-state quant (scaled_fp8_quant, use_per_token_if_dynamic=True) ----
+
+HQ = P.fp8_hidden_quant
+TOKEN_GRID = [(r, k, s) for r in (1, 5, 20, 64, 2048) for k in (2560,) for s in (1.0, 1e-3, 60.0)]
+# widths at the register kernel's bounds (1024 / 2048 / 3072 / 4096), past them (two-pass),
+# unaligned (K % 8 != 0) and tiny
+TOKEN_GRID += [(33, k, 1.0) for k in (7, 8, 128, 1024, 1032, 2048, 3072, 4096, 4104, 8192)]
+
+
+@pytest.mark.parametrize("rows,K,sc", TOKEN_GRID)
+def test_per_token_quant_bit_exact(cuda, rows, K, sc):
+    torch.manual_seed(rows * 13 + K)
+    x = torch.randn(rows, K, device=cuda, dtype=torch.bfloat16) * sc
+    if rows > 1:
+        x[1] = 0.0                                             # the min-scale floor
+    q, s = HQ.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+    rq, rs = Q.per_token_quant_fp8(x)
+    assert s.shape == (rows, 1) and _eq(s, rs) and _eq(q, rq)
+
+
+def test_per_token_quant_f16_strided_scale_ub(cuda):
+    torch.manual_seed(5)
+    big = torch.randn(20, 2560 + 8, device=cuda, dtype=torch.float16) * 4
+    x = big[:, :2560]                                          # row stride 2568
+    q, s = HQ.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+    rq, rs = Q.per_token_quant_fp8(x)
+    assert _eq(q, rq) and _eq(s, rs)
+    ub = torch.tensor([2.0], device=cuda)
+    q, s = HQ.scaled_fp8_quant(x, use_per_token_if_dynamic=True, scale_ub=ub)
+    rq, rs = Q.per_token_quant_fp8(x, ub)
+    assert _eq(q, rq) and _eq(s, rs)
+    unal = torch.randn(20 * 2560 + 1, device=cuda, dtype=torch.bfloat16)[1:].view(20, 2560)
+    q, s = HQ.scaled_fp8_quant(unal, use_per_token_if_dynamic=True)
+    rq, rs = Q.per_token_quant_fp8(unal)
+    assert _eq(q, rq) and _eq(s, rs)
+
+
+def test_per_token_quant_matches_vllm_op(cuda):
+    """Against vLLM's own scaled_fp8_quant(use_per_token_if_dynamic=True) where it loads."""
+    try:
+        from vllm import _custom_ops as ops
+        ops.scaled_fp8_quant(torch.randn(2, 64, device=cuda, dtype=torch.bfloat16),
+                             use_per_token_if_dynamic=True)
+    except Exception as e:  # noqa: BLE001
+        pytest.skip(f"vLLM _C ops unavailable here: {type(e).__name__}")
+    for rows in (1, 20, 64, 2048):
+        x = torch.randn(rows, 2560, device=cuda, dtype=torch.bfloat16)
+        qr, sr = ops.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+        q, s = HQ.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+        nd = int((q.view(torch.uint8) != qr.view(torch.uint8)).sum())
+        print(f"rows={rows}: scale equal {torch.equal(s, sr)}, q diffs {nd}")
+        assert torch.equal(s, sr) and nd == 0, rows
+
+
+def test_fp8_quant_shared_reuses_on_gpu(cuda):
+    x = torch.randn(20, 2560, device=cuda, dtype=torch.bfloat16)
+    HQ.set_share(True)
+    try:
+        a = HQ.fp8_quant_shared(x)
+        b = HQ.fp8_quant_shared(x)
+        assert a[0] is b[0]
+        c = HQ.fp8_quant_shared(x)
+        assert c[0] is not a[0] and _eq(c[0], a[0]) and _eq(c[1], a[1])
+    finally:
+        HQ.set_share(False)
