@@ -37,9 +37,9 @@ int b200_gemv_sigmoid_gate_mul(void* y, const void* out, const void* x, const vo
  * (patches/model_executor/layers/fused_moe/experts/r4d_mxfp4_moe.py.lru.diff L638, L696):
  * out[t, :] = sum_k in[t, k, :]. in [tokens, topk, H] contiguous; out [tokens, H] with row
  * stride stride_out. top_k in {2, 3, 4}: the running sum is rounded to dtype after every add
- * (vLLM's kernel keeps it in the storage type); any other top_k: fp32 accumulation in k order
- * and one rounding (torch.sum over the top_k axis). -1: tokens or H < 0, topk outside
- * [1, 32], stride_out < H; -2: bad dtype. */
+ * (vLLM's kernel keeps it in the storage type); any other top_k: torch.sum's CUDA order, four
+ * fp32 accumulators over k = i mod 4 combined as ((a0 + a1) + a2) + a3, one rounding.
+ * -1: tokens or H < 0, topk outside [1, 32], stride_out < H; -2: bad dtype. */
 int b200_moe_sum(const void* in, void* out, int tokens, int topk, int H, long long stride_out,
                  int dtype, cudaStream_t stream);
 

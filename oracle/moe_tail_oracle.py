@@ -69,15 +69,20 @@ def ulp_neighbours(g: torch.Tensor) -> list[torch.Tensor]:
 
 
 def moe_sum(x: torch.Tensor, round_each: bool | None = None) -> torch.Tensor:
-    """[T, top_k, H] -> [T, H], summed over top_k in k order. ``round_each`` (default: top_k in
-    {2, 3, 4}, vLLM's storage-dtype kernel) rounds the running sum to x's dtype after every
-    add; otherwise the sum is fp32 with one rounding (torch.sum over the top_k axis)."""
+    """[T, top_k, H] -> [T, H]. ``round_each`` (default: top_k in {2, 3, 4}, vLLM's
+    storage-dtype kernel) adds the rows in k order and rounds the running sum to x's dtype after
+    every add. Otherwise torch.sum's CUDA order for this layout (ATen native/cuda/Reduce.cuh,
+    thread_reduce_impl, vt0 = 4): fp32 accumulators a_i over k = i, i + 4, ..., combined as
+    ((a0 + a1) + a2) + a3 and rounded once."""
     topk = x.shape[1]
     if round_each is None:
         round_each = 2 <= topk <= 4
-    acc = torch.zeros(x.shape[0], x.shape[2], dtype=torch.float32, device=x.device)
+    if round_each:
+        acc = torch.zeros(x.shape[0], x.shape[2], dtype=torch.float32, device=x.device)
+        for k in range(topk):
+            acc = (acc + x[:, k].float()).to(x.dtype).float()
+        return acc.to(x.dtype)
+    accs = [torch.zeros(x.shape[0], x.shape[2], dtype=torch.float32, device=x.device) for _ in range(4)]
     for k in range(topk):
-        acc = acc + x[:, k].float()
-        if round_each:
-            acc = acc.to(x.dtype).float()
-    return acc.to(x.dtype)
+        accs[k % 4] = accs[k % 4] + x[:, k].float()
+    return (((accs[0] + accs[1]) + accs[2]) + accs[3]).to(x.dtype)

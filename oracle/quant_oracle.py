@@ -42,6 +42,20 @@ W4_GROUP = 128                             # draft_w4_lmhead.py:70
 CLIP_GRID = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7, 0.65, 0.6)   # draft_w4_lmhead.py:151
 
 
+def _amax_rows(xf: torch.Tensor, dim, keepdim: bool = False) -> torch.Tensor:
+    """max |x| along `dim` with NaNs ignored (the kernels' and the reference's fmax-based
+    reduction: fmax(m, NaN) = m)."""
+    a = xf.abs()
+    return torch.where(torch.isnan(a), torch.zeros_like(a), a).amax(dim=dim, keepdim=keepdim)
+
+
+def _clamp_fp8(v: torch.Tensor) -> torch.Tensor:
+    """maximum(-448, minimum(v, 448)) with C fmin / fmax semantics (fused_silu_mul_quant.py:56,
+    vLLM's fmaxf(-max, fminf(v, max))): a NaN becomes +448."""
+    hi = torch.full_like(v, FP8_MAX)
+    return torch.fmax(torch.fmin(v, hi), -hi)
+
+
 # ---------------------------------------------------------------------------------------
 # fused SiLU * mul -> FP8
 # ---------------------------------------------------------------------------------------
@@ -62,11 +76,11 @@ def silu_mul_quant(x: torch.Tensor, write_act: bool = False):
     ``max(amax/448, 1/(448*512))`` and a true division (fused_silu_mul_quant.py:51-57)."""
     a = silu_mul(x)
     af = a.float()
-    amax = af.abs().amax(dim=1, keepdim=True) if af.shape[1] else af.new_zeros(af.shape[0], 1)
+    amax = _amax_rows(af, 1, keepdim=True) if af.shape[1] else af.new_zeros(af.shape[0], 1)
     # a true division by 448: a tensor divisor (torch turns a Python-scalar divisor into a
     # reciprocal multiply on CUDA, which is not the reference's `amax / FP8_MAX`)
     scale = torch.clamp_min(amax / torch.full_like(amax, FP8_MAX), MIN_SCALE)
-    q = (af / scale).clamp(-FP8_MAX, FP8_MAX).to(FP8)
+    q = _clamp_fp8(af / scale).to(FP8)
     return (a if write_act else None), q, scale
 
 
@@ -74,9 +88,9 @@ def group_quant_fp8(x: torch.Tensor, group: int = BLK, eps: float = GROUP_EPS):
     """Per-token group quant: (q e4m3 [M, K], scale fp32 [M, K/group]) row-major."""
     M, K = x.shape
     xf = x.float().reshape(M, K // group, group)
-    amax = torch.clamp_min(xf.abs().amax(dim=-1), eps)
+    amax = torch.clamp_min(_amax_rows(xf, -1), eps)
     s = amax * torch.full_like(amax, 1.0 / FP8_MAX)          # amax * fp32(1/448)
-    q = (xf / s.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(FP8).reshape(M, K)
+    q = _clamp_fp8(xf / s.unsqueeze(-1)).to(FP8).reshape(M, K)
     return q, s.contiguous()
 
 
@@ -85,11 +99,11 @@ def per_token_quant_fp8(x: torch.Tensor, scale_ub: torch.Tensor | None = None):
     it (r4dhip.py.diff L19-34): row amax (capped by ``scale_ub``), scale = max(amax / 448,
     1/(448*512)) with a true division, q = e4m3(clamp(x / scale)). -> (q [M, K], scale [M, 1])."""
     xf = x.float()
-    amax = xf.abs().amax(dim=1, keepdim=True) if xf.shape[1] else xf.new_zeros(xf.shape[0], 1)
+    amax = _amax_rows(xf, 1, keepdim=True) if xf.shape[1] else xf.new_zeros(xf.shape[0], 1)
     if scale_ub is not None:
-        amax = torch.minimum(amax, scale_ub.float().reshape(1, 1).to(amax.device))
+        amax = torch.fmin(amax, scale_ub.float().reshape(1, 1).to(amax.device))
     scale = torch.clamp_min(amax / torch.full_like(amax, FP8_MAX), MIN_SCALE)
-    q = (xf / scale).clamp(-FP8_MAX, FP8_MAX).to(FP8)
+    q = _clamp_fp8(xf / scale).to(FP8)
     return q, scale
 
 

@@ -167,10 +167,10 @@ __device__ void load_activation(const Params& p, char* sm, int rows_x, uint64_t*
       for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
       const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
       uint2 b;
-      b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
-                             fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
-      b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
-                             fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+      b.x = b200::pack4_e4m3(fmaxf(fminf(f[0] / sc, 448.f), -448.f), fmaxf(fminf(f[1] / sc, 448.f), -448.f),
+                             fmaxf(fminf(f[2] / sc, 448.f), -448.f), fmaxf(fminf(f[3] / sc, 448.f), -448.f));
+      b.y = b200::pack4_e4m3(fmaxf(fminf(f[4] / sc, 448.f), -448.f), fmaxf(fminf(f[5] / sc, 448.f), -448.f),
+                             fmaxf(fminf(f[6] / sc, 448.f), -448.f), fmaxf(fminf(f[7] / sc, 448.f), -448.f));
       *reinterpret_cast<uint2*>(dst) = b;
       if (hl == 0) xs[m * KB + kb] = sc;
       if (p.qx_out != nullptr && blockIdx.x == 0) {
@@ -651,10 +651,10 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
       for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
       sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
-      b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
-                             fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
-      b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
-                             fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+      b.x = b200::pack4_e4m3(fmaxf(fminf(f[0] / sc, 448.f), -448.f), fmaxf(fminf(f[1] / sc, 448.f), -448.f),
+                             fmaxf(fminf(f[2] / sc, 448.f), -448.f), fmaxf(fminf(f[3] / sc, 448.f), -448.f));
+      b.y = b200::pack4_e4m3(fmaxf(fminf(f[4] / sc, 448.f), -448.f), fmaxf(fminf(f[5] / sc, 448.f), -448.f),
+                             fmaxf(fminf(f[6] / sc, 448.f), -448.f), fmaxf(fminf(f[7] / sc, 448.f), -448.f));
       if (qx_out != nullptr) {
         *reinterpret_cast<uint2*>(qx_out + (long long)m * K + kb * 128 + hl * 8) = b;
         if (hl == 0) xs_out[m * KB + kb] = sc;
@@ -693,10 +693,10 @@ __global__ void __launch_bounds__(128)
   for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(hmask, amax, o));
   const float sc = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
   uint2 b;
-  b.x = b200::pack4_e4m3(fminf(fmaxf(f[0] / sc, -448.f), 448.f), fminf(fmaxf(f[1] / sc, -448.f), 448.f),
-                         fminf(fmaxf(f[2] / sc, -448.f), 448.f), fminf(fmaxf(f[3] / sc, -448.f), 448.f));
-  b.y = b200::pack4_e4m3(fminf(fmaxf(f[4] / sc, -448.f), 448.f), fminf(fmaxf(f[5] / sc, -448.f), 448.f),
-                         fminf(fmaxf(f[6] / sc, -448.f), 448.f), fminf(fmaxf(f[7] / sc, -448.f), 448.f));
+  b.x = b200::pack4_e4m3(fmaxf(fminf(f[0] / sc, 448.f), -448.f), fmaxf(fminf(f[1] / sc, 448.f), -448.f),
+                         fmaxf(fminf(f[2] / sc, 448.f), -448.f), fmaxf(fminf(f[3] / sc, 448.f), -448.f));
+  b.y = b200::pack4_e4m3(fmaxf(fminf(f[4] / sc, 448.f), -448.f), fmaxf(fminf(f[5] / sc, 448.f), -448.f),
+                         fmaxf(fminf(f[6] / sc, 448.f), -448.f), fmaxf(fminf(f[7] / sc, 448.f), -448.f));
   *reinterpret_cast<uint2*>(qr + (long long)m * K + kb * 128 + hl * 8) = b;
   if (hl == 0) sr[m * KB + kb] = sc;
 }

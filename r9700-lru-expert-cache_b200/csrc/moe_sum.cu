@@ -4,9 +4,12 @@
 // `ops.moe_sum(ic3.view(M, top_k, H), output)`), for sm_100a.
 //
 // Rounding follows vLLM's op: for top_k in {2, 3, 4} its kernel keeps the running sum in the
-// storage dtype (each `x += in[k]` is an fp32 add rounded back to the dtype), for any other
-// top_k it is torch.sum over the top_k axis (fp32 accumulation in k order, one rounding).
-// ROUND_EACH selects the first form.
+// storage dtype (each `x += in[k]` is an fp32 add rounded back to the dtype; ROUND_EACH). For
+// any other top_k it is torch.sum over the top_k axis, whose CUDA reduction (ATen
+// native/cuda/Reduce.cuh, thread_reduce_impl with vt0 = 4) gives each output thread four fp32
+// accumulators: a_i sums the rows k = i, i + 4, i + 8, ... in order, and the result is
+// ((a0 + a1) + a2) + a3, rounded once. For this layout (the top_k axis is not the fastest
+// moving one) and top_k <= 32 no thread splits the top_k axis, so that order is the whole sum.
 //
 // B200 mapping: HBM-bound (top_k * 2 bytes read + 2 written per output element). One thread
 // per 16-byte chunk of a token's output row: it issues its top_k 16-byte loads at once (the
@@ -55,48 +58,56 @@ __global__ void __launch_bounds__(MS_THREADS)
   const unsigned long long t = i / per_row;
   const unsigned c = (unsigned)(i - t * per_row);
   const T* src = in + (t * topk) * (unsigned long long)H + (unsigned long long)c * E;
-  float acc[E];
+  // ROUND_EACH: one running sum (acc[0]); otherwise four interleaved accumulators
+  float acc[4][E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  if constexpr (VEC) {
-    constexpr int KU = TOPK_C > 0 ? TOPK_C : 1;
-    if constexpr (TOPK_C > 0) {
-      uint4 v[KU];
+  for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int k = 0; k < KU; ++k) v[k] = __ldg(reinterpret_cast<const uint4*>(src + (long long)k * H));
+    for (int e = 0; e < E; ++e) acc[a][e] = 0.f;
+  // row k goes to accumulator k & 3; every call below has a compile-time accumulator index
+  auto add = [&](int a, const T* p) {
+    if (ROUND_EACH) a = 0;
 #pragma unroll
-      for (int k = 0; k < KU; ++k) {
-        const T* p = reinterpret_cast<const T*>(&v[k]);
+    for (int e = 0; e < E; ++e) {
+      acc[a][e] += to_f(p[e]);
+      if (ROUND_EACH) acc[a][e] = to_f(from_f<T>(acc[a][e]));
+    }
+  };
+  if constexpr (VEC && TOPK_C > 0) {
+    uint4 v[TOPK_C];
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          acc[e] += to_f(p[e]);
-          if (ROUND_EACH) acc[e] = to_f(from_f<T>(acc[e]));
-        }
-      }
-    } else {
-      for (int k = 0; k < topk; ++k) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + (long long)k * H));
-        const T* p = reinterpret_cast<const T*>(&v);
+    for (int k = 0; k < TOPK_C; ++k) v[k] = __ldg(reinterpret_cast<const uint4*>(src + (long long)k * H));
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          acc[e] += to_f(p[e]);
-          if (ROUND_EACH) acc[e] = to_f(from_f<T>(acc[e]));
+    for (int k = 0; k < TOPK_C; ++k) add(k & 3, reinterpret_cast<const T*>(&v[k]));
+  } else {
+    for (int k0 = 0; k0 < topk; k0 += 4) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int k = k0 + a;
+        if (k < topk) {
+          if constexpr (VEC) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + (long long)k * H));
+            add(a, reinterpret_cast<const T*>(&v));
+          } else {
+            add(a, src + (long long)k * H);
+          }
         }
       }
     }
-    union {
-      uint4 raw;
-      T v[E];
-    } o;
+  }
+  union {
+    uint4 raw;
+    T v[E];
+  } o;
 #pragma unroll
-    for (int e = 0; e < E; ++e) o.v[e] = from_f<T>(acc[e]);
+  for (int e = 0; e < E; ++e) {
+    const float r = ROUND_EACH ? acc[0][e] : ((acc[0][e] + acc[1][e]) + acc[2][e]) + acc[3][e];
+    o.v[e] = from_f<T>(r);
+  }
+  if constexpr (VEC) {
     *reinterpret_cast<uint4*>(out + t * (unsigned long long)stride_out + (unsigned long long)c * E) = o.raw;
   } else {
-    for (int k = 0; k < topk; ++k) {
-      acc[0] += to_f(src[(long long)k * H]);
-      if (ROUND_EACH) acc[0] = to_f(from_f<T>(acc[0]));
-    }
-    out[t * (unsigned long long)stride_out + c] = from_f<T>(acc[0]);
+    out[t * (unsigned long long)stride_out + c] = o.v[0];
   }
 }
 

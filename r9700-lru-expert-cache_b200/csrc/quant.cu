@@ -5,7 +5,9 @@
 //   (the storage-dtype rounding of vLLM's act_and_mul_kernel), amax = max |a|,
 //   scale = max(amax / 448, 1 / (448 * 512)), q = e4m3(clamp(a / scale, +-448)) -- a true
 //   IEEE division, not a reciprocal multiply (fused_silu_mul_quant.py:9-14). Built without
-//   fast math so `/` and expf are the IEEE / accurate forms.
+//   fast math so `/` and expf are the IEEE / accurate forms. The clamp is the reference's
+//   maximum(-448, minimum(v, 448)) (fused_silu_mul_quant.py:56), whose fmin-first order sends
+//   a NaN to +448; the row amax ignores NaNs as fmax does.
 //   The group variant (group = 128) replaces the per-row scale with one per 128 columns,
 //   following per_token_group_quant_fp8: scale = max(amax, 1e-10) * fp32(1/448).
 //
@@ -111,7 +113,7 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float af = silu_mul_elem<T>(g[i], u[i], &a[i]);
-        b[i] = b200::f32_to_e4m3(fminf(fmaxf(af / sc, -kFp8Max), kFp8Max));
+        b[i] = b200::f32_to_e4m3(fmaxf(fminf(af / sc, kFp8Max), -kFp8Max));
       }
       uint8_t* qp = q + (long long)row * d + 8 * c;
       if (VEC) {
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
       if ((lane & 15) == 0) scale[(long long)row * ngroups + grp] = sc;
       uint8_t b[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(af[i] / sc, -kFp8Max), kFp8Max));
+      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fmaxf(fminf(af[i] / sc, kFp8Max), -kFp8Max));
       *reinterpret_cast<uint2*>(q + (long long)row * d + 8 * c) = *reinterpret_cast<const uint2*>(b);
     }
   }
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
     if (c < nchunk) {
       uint8_t b[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(af[j][i] / sc, -kFp8Max), kFp8Max));
+      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fmaxf(fminf(af[j][i] / sc, kFp8Max), -kFp8Max));
       *reinterpret_cast<uint2*>(q + (long long)row * d + 8 * c) = *reinterpret_cast<const uint2*>(b);
     }
   }
@@ -206,39 +208,50 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
 // Per-token dynamic FP8 quant of a [rows, K] activation (vLLM scaled_fp8_quant with
 // use_per_token_if_dynamic=True): amax = max |x| over the row, clipped to *scale_ub when
 // given, scale = max(amax / 448, 1 / (448 * 512)), q = e4m3(clamp(x / scale, +-448)) with a
-// true division. One warp per row. RC > 0: the row (16-byte aligned, K % 8 == 0, at most
-// 256 * RC elements) stays in registers as raw 16-byte chunks between the amax and the
-// quantization, so HBM is read once; RC == 0: two passes over the row (the second is served
-// by L1 / L2), for wide or unaligned rows.
-template <typename T, int RC, bool VEC>
-__global__ void __launch_bounds__(32 * ROWS_PER_CTA)
+// true division.
+//
+// WPR warps per row, 256-thread CTAs (256 / (32 * WPR) rows each). RC > 0: the row (16-byte
+// aligned, K % 8 == 0, at most 256 * WPR * RC elements) stays in registers as raw 16-byte
+// chunks between the amax and the quantization, so HBM is read once; chunk c of the row goes
+// to thread c % (32 * WPR) of its row group. RC is kept <= 4 so the kernel runs at full
+// occupancy and the warps of an SM overlap their loads with one another's arithmetic. RC == 0:
+// two passes over the row (the second served by L1 / L2), for wide or unaligned rows. The
+// row amax of several warps meets in shared memory.
+constexpr int TQ_THREADS = 256;
+
+template <typename T, int WPR, int RC, bool VEC>
+__global__ void __launch_bounds__(TQ_THREADS)
     token_quant_kernel(const T* __restrict__ x, long long stride_x, int rows, int K,
                        const float* __restrict__ scale_ub, uint8_t* __restrict__ q,
                        float* __restrict__ scale) {
-  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
-  const T* xr = x + (long long)row * stride_x;
-  uint8_t* qr = q + (long long)row * K;
+  constexpr int RPC = TQ_THREADS / (32 * WPR);              // rows per CTA
+  constexpr int TPR = 32 * WPR;                              // threads per row
+  __shared__ float s_amax[TQ_THREADS / 32];
+  const int warp = threadIdx.x >> 5;
+  const int rit = threadIdx.x % TPR;                         // thread index within the row
+  const int row = blockIdx.x * RPC + threadIdx.x / TPR;
+  const bool live = row < rows;                              // every thread reaches the barrier
+  const T* xr = x + (long long)(live ? row : 0) * stride_x;
+  uint8_t* qr = q + (long long)(live ? row : 0) * K;
   const int nchunk = (K + 7) / 8;
   float amax = 0.f;
   uint4 keep[RC > 0 ? RC : 1];
   if constexpr (RC > 0) {
 #pragma unroll
     for (int j = 0; j < RC; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nchunk) keep[j] = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+      const int c = rit + TPR * j;
+      if (live && c < nchunk) keep[j] = __ldg(reinterpret_cast<const uint4*>(xr) + c);
     }
 #pragma unroll
     for (int j = 0; j < RC; ++j) {
-      if (lane + 32 * j < nchunk) {
+      if (live && rit + TPR * j < nchunk) {
         const T* v = reinterpret_cast<const T*>(&keep[j]);
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(to_f(v[i])));
       }
     }
-  } else {
-    for (int c = lane; c < nchunk; c += 32) {
+  } else if (live) {
+    for (int c = rit; c < nchunk; c += TPR) {
       T v[8];
       load8<T, VEC>(xr + 8 * c, min(8, K - 8 * c), v);
 #pragma unroll
@@ -246,29 +259,37 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
     }
   }
   amax = b200::warp_max(amax);
+  if constexpr (WPR > 1) {
+    if ((threadIdx.x & 31) == 0) s_amax[warp] = amax;
+    __syncthreads();
+    const int w0 = (warp / WPR) * WPR;
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, s_amax[w0 + w]);
+  }
+  if (!live) return;
   if (scale_ub != nullptr) amax = fminf(amax, *scale_ub);
   const float sc = fmaxf(amax / kFp8Max, kMinScale);
-  if (lane == 0) scale[row] = sc;
+  if (rit == 0) scale[row] = sc;
   if constexpr (RC > 0) {
 #pragma unroll
     for (int j = 0; j < RC; ++j) {
-      const int c = lane + 32 * j;
+      const int c = rit + TPR * j;
       if (c < nchunk) {
         const T* v = reinterpret_cast<const T*>(&keep[j]);
         uint8_t b[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(to_f(v[i]) / sc, -kFp8Max), kFp8Max));
+        for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fmaxf(fminf(to_f(v[i]) / sc, kFp8Max), -kFp8Max));
         *reinterpret_cast<uint2*>(qr + 8 * c) = *reinterpret_cast<const uint2*>(b);
       }
     }
   } else {
-    for (int c = lane; c < nchunk; c += 32) {
+    for (int c = rit; c < nchunk; c += TPR) {
       const int nv = min(8, K - 8 * c);
       T v[8];
       load8<T, VEC>(xr + 8 * c, nv, v);
       uint8_t b[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(to_f(v[i]) / sc, -kFp8Max), kFp8Max));
+      for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fmaxf(fminf(to_f(v[i]) / sc, kFp8Max), -kFp8Max));
       if (VEC) {
         *reinterpret_cast<uint2*>(qr + 8 * c) = *reinterpret_cast<const uint2*>(b);
       } else {
@@ -278,28 +299,50 @@ __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
   }
 }
 
+template <typename T, int WPR>
+void launch_tq_wpr(const T* xp, long long stride_x, int rows, int K, const float* ub, uint8_t* qp,
+                   float* scale, int rc, cudaStream_t stream) {
+  constexpr int RPC = TQ_THREADS / (32 * WPR);
+  const dim3 grid((rows + RPC - 1) / RPC), block(TQ_THREADS);
+  if (rc == 1)
+    token_quant_kernel<T, WPR, 1, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (rc == 2)
+    token_quant_kernel<T, WPR, 2, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else if (rc == 3)
+    token_quant_kernel<T, WPR, 3, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  else
+    token_quant_kernel<T, WPR, 4, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+}
+
 template <typename T>
 int launch_token_quant(const void* x, long long stride_x, int rows, int K, const float* ub,
                        void* q, float* scale, cudaStream_t stream) {
   const bool vec = (K % 8 == 0) && (stride_x % 8 == 0) &&
                    ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                    ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
-  const dim3 grid((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA), block(32 * ROWS_PER_CTA);
   const T* xp = static_cast<const T*>(x);
   uint8_t* qp = static_cast<uint8_t*>(q);
   const int nchunk = K / 8;
-  if (vec && nchunk <= 32 * 4)
-    token_quant_kernel<T, 4, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
-  else if (vec && nchunk <= 32 * 8)
-    token_quant_kernel<T, 8, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
-  else if (vec && nchunk <= 32 * 12)
-    token_quant_kernel<T, 12, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
-  else if (vec && nchunk <= 32 * 16)
-    token_quant_kernel<T, 16, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
-  else if (vec)
-    token_quant_kernel<T, 0, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
-  else
-    token_quant_kernel<T, 0, false><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  if (vec && nchunk <= 32 * 8 * 4) {
+    // the fewest warps per row that keep RC <= 4, then more while the grid has fewer CTAs
+    // than SMs (decode-sized row counts spread over more of the chip)
+    int wpr = 1;
+    while (wpr < 8 && nchunk > 32 * wpr * 4) wpr *= 2;
+    while (wpr < 8 && (long long)rows * wpr * 32 < (long long)TQ_THREADS * 148) wpr *= 2;
+    const int rc = (nchunk + 32 * wpr - 1) / (32 * wpr);
+    switch (wpr) {
+      case 1: launch_tq_wpr<T, 1>(xp, stride_x, rows, K, ub, qp, scale, rc, stream); break;
+      case 2: launch_tq_wpr<T, 2>(xp, stride_x, rows, K, ub, qp, scale, rc, stream); break;
+      case 4: launch_tq_wpr<T, 4>(xp, stride_x, rows, K, ub, qp, scale, rc, stream); break;
+      default: launch_tq_wpr<T, 8>(xp, stride_x, rows, K, ub, qp, scale, rc, stream); break;
+    }
+  } else {
+    const dim3 grid(rows), block(TQ_THREADS);               // one row per CTA, two passes
+    if (vec)
+      token_quant_kernel<T, 8, 0, true><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+    else
+      token_quant_kernel<T, 8, 0, false><<<grid, block, 0, stream>>>(xp, stride_x, rows, K, ub, qp, scale);
+  }
   return (int)cudaGetLastError();
 }
 
@@ -334,7 +377,7 @@ __global__ void __launch_bounds__(256)
     if (kc % cpg == 0) s[(long long)m * ng + kc / cpg] = sc;
     uint8_t b[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fminf(fmaxf(f[i] / sc, -kFp8Max), kFp8Max));
+    for (int i = 0; i < 8; ++i) b[i] = b200::f32_to_e4m3(fmaxf(fminf(f[i] / sc, kFp8Max), -kFp8Max));
     *reinterpret_cast<uint2*>(q + (long long)m * K + 8 * kc) = *reinterpret_cast<const uint2*>(b);
   }
 }

@@ -4,8 +4,11 @@ L638, L696: ``ops.moe_sum(ic3.view(M, top_k, H), output)``), with vLLM's signatu
 rounding, backed by the sm_100a kernel ``b200_moe_sum`` in csrc/moe_sum.cu.
 
 Rounding: for top_k in {2, 3, 4} the running sum is rounded to the storage dtype after every
-add (vLLM's kernel keeps it in that type); for any other top_k the sum is fp32 in k order
-with one rounding (vLLM falls back to torch.sum over the top_k axis).
+add (vLLM's kernel keeps it in that type); for any other top_k vLLM falls back to torch.sum
+over the top_k axis, whose CUDA reduction keeps four interleaved fp32 accumulators
+(k = i mod 4) combined as ((a0 + a1) + a2) + a3 and rounds once; the kernel sums in that order.
+For H = 1 torch splits the top_k axis across threads instead, an order this kernel does not
+follow.
 """
 from __future__ import annotations
 

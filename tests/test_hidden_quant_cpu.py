@@ -108,3 +108,18 @@ def test_per_token_entry_codes_and_forms():
     if not torch.cuda.is_available():
         with pytest.raises(ValueError):
             HQ.scaled_fp8_quant(x, use_per_token_if_dynamic=True)   # no CPU fallback
+
+
+def test_non_finite_inputs_follow_the_reference_clamp():
+    """maximum(-448, minimum(v, 448)) (fused_silu_mul_quant.py:56; vLLM's fmaxf(-max,
+    fminf(v, max))): NaN -> +448 (0x7E), +-inf -> +-448; the row amax ignores NaNs."""
+    x = torch.tensor([[1.0, float("nan"), -2.0, 0.5]], dtype=torch.bfloat16)
+    q, s = Q.per_token_quant_fp8(x)
+    assert s.item() == pytest.approx(2.0 / 448.0)
+    assert q.view(torch.uint8).tolist()[0][1] == 0x7E
+    assert q.view(torch.uint8).tolist()[0][2] == 0xFE                 # -2 / (2/448) = -448
+    q, s = Q.per_token_quant_fp8(x, torch.tensor([1.0]))               # capped: -2 clamps
+    assert q.view(torch.uint8).tolist()[0][2] == 0xFE
+    y = torch.tensor([[float("-inf"), 1.0]], dtype=torch.bfloat16)
+    q, s = Q.per_token_quant_fp8(y)                                    # inf amax -> inf scale
+    assert s.item() == float("inf") and q.view(torch.uint8).tolist()[0] == [0x7E, 0x00]

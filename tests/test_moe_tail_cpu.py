@@ -107,13 +107,22 @@ def test_gate_ops_fail_loudly_without_gpu():
 
 # ---- moe_sum ----
 
-def test_moe_sum_oracle_matches_torch_sum_for_wide_topk():
-    """top_k outside {2, 3, 4}: fp32 sum with one rounding, which torch.sum over the top_k axis
-    also gives on CPU for these sizes."""
+def test_moe_sum_oracle_wide_topk_order():
+    """top_k outside {2, 3, 4}: four interleaved fp32 accumulators, ((a0 + a1) + a2) + a3.
+    Rows [e, e, e, e, 1] (f32, e = 2^-24) tell the orders apart: in k order the four e sum to
+    4e exactly and 1 + 4e = 1 + 2^-22 is representable; in torch's order a0 = e + 1 rounds to
+    1 and every later e is lost against 1."""
+    e = 2.0 ** -24
+    x = torch.tensor([[[e], [e], [e], [e], [1.0]]], dtype=torch.float32)
+    assert G.moe_sum(x).item() == 1.0
+    seq = torch.tensor(0.0)
+    for k in range(5):
+        seq = seq + x[0, k, 0]
+    assert seq.item() == 1.0 + 2.0 ** -22
     torch.manual_seed(4)
     for topk in (1, 5, 8, 10):
-        x = torch.randn(20, topk, G.H, dtype=torch.bfloat16)
-        assert torch.equal(G.moe_sum(x), x.sum(dim=1)), topk
+        xb = torch.randn(20, topk, G.H, dtype=torch.bfloat16)
+        assert torch.equal(G.moe_sum(xb), xb.sum(dim=1)), topk      # torch's CPU sum agrees here
 
 
 def test_moe_sum_oracle_rounds_each_add_for_small_topk():

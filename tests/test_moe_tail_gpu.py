@@ -207,6 +207,16 @@ def test_moe_sum_dtypes_and_strided_out(cuda, dt):
     assert big[:, G.H:].eq(0).all()                          # nothing written past the row
 
 
+def test_moe_sum_follows_torch_reduction_order(cuda):
+    """The case that separates torch's four-accumulator order from a k-order sum (rows
+    [e, e, e, e, 1], e = 2^-24, f32): the kernel, the oracle and torch.sum all give 1."""
+    e = 2.0 ** -24
+    x = torch.tensor([e, e, e, e, 1.0], device=cuda).view(1, 5, 1).expand(3, 5, 8).contiguous()
+    out = torch.empty(3, 8, device=cuda)
+    MS.moe_sum(x, out)
+    assert out.eq(1.0).all() and _same(out, x.sum(dim=1)) and _same(out, G.moe_sum(x))
+
+
 def test_moe_sum_matches_vllm_op(cuda):
     """Against vLLM's own ops.moe_sum where it loads (both rounding forms reported)."""
     try:

@@ -215,3 +215,30 @@ def test_fp8_quant_shared_reuses_on_gpu(cuda):
         assert c[0] is not a[0] and _eq(c[0], a[0]) and _eq(c[1], a[1])
     finally:
         HQ.set_share(False)
+
+
+def test_non_finite_rows_match_oracle(cuda):
+    """NaN / inf values through all three quant kernels: the reference's clamp order sends NaN
+    to +448, infinities saturate, and the row / group amax ignores NaNs."""
+    torch.manual_seed(11)
+    x = torch.randn(6, 2 * 512, device=cuda, dtype=torch.bfloat16)
+    x[0, 5] = float("nan")
+    x[1, 7] = float("inf")
+    x[2, 600] = float("-inf")
+    x[3, 9] = float("nan")
+    x[3, 700] = float("nan")
+    act, q, s = FQ.silu_mul_quant(x, FP8, write_act=True)
+    ra, rq, rs = Q.silu_mul_quant(x, write_act=True)
+    # NaN payloads of the activation may differ between conversions: compare NaN positions
+    assert torch.equal(act.isnan(), ra.isnan()) and torch.equal(act.nan_to_num(), ra.nan_to_num())
+    assert _eq(q, rq)
+    assert torch.equal(s.isnan(), rs.isnan()) and torch.equal(s.nan_to_num(), rs.nan_to_num())
+    h = torch.randn(6, 2560, device=cuda, dtype=torch.bfloat16)
+    h[0, 3], h[1, 1000], h[2, 2559], h[4, 0] = float("nan"), float("inf"), float("-inf"), float("nan")
+    for ub in (None, torch.tensor([2.0], device=cuda)):
+        hq, hs = HQ.scaled_fp8_quant(h, use_per_token_if_dynamic=True, scale_ub=ub)
+        rq, rs = Q.per_token_quant_fp8(h, ub)
+        assert _eq(hq, rq) and torch.equal(hs, rs)
+    gq, gs = FQ.per_token_group_quant_fp8(h, 128)
+    rq, rs = Q.group_quant_fp8(h, 128)
+    assert _eq(gq, rq) and torch.equal(gs, rs)
