@@ -92,7 +92,19 @@ struct Params {
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
   int kw;            // tcgen05 path: 128-K blocks per stage
   float* px;         // tcgen05 path: partial accumulators of blocks split along K
+  int tc_fin;        // tcgen05 path: 1 = split pairs finished inside the kernel (no finish kernel)
+  int* flags;        // tcgen05 path, tc_fin: per-CTA count of epilogue warps that published
 };
+
+// Release / acquire on a gpu-scope counter (the in-kernel finish of split tcgen05 pairs).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 template <int NC>
 __device__ __forceinline__ void consumer_bar() {
@@ -626,8 +638,12 @@ __global__ void __launch_bounds__(128)
     act_tiles_kernel(const __nv_bfloat16* __restrict__ x, const uint8_t* __restrict__ qx_in,
                      const float* __restrict__ xs_in, int M, int K, int tpad,
                      uint8_t* __restrict__ qt, float* __restrict__ xt, uint8_t* __restrict__ qx_out,
-                     float* __restrict__ xs_out) {
+                     float* __restrict__ xs_out, int* __restrict__ flags, int nflags) {
   griddep_launch_dependents();              // the GEMM may start streaming weights now
+  // the GEMM's publish counters start every call at zero (this kernel is stream-ordered after
+  // the previous call, and the GEMM touches them only after griddepcontrol.wait)
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0;
   const int KB = K / 128, kb = blockIdx.x;
   const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
   const unsigned hmask = 0xffffu << (16 * (hw & 1));
@@ -1003,14 +1019,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
         if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
       }
-      if (j0 != 0 || j1 != wk.KBS - 1) {
+      const bool head_split = j0 != 0, tail_split = j1 != wk.KBS - 1;
+      if (head_split || (tail_split && !p.tc_fin)) {
         // A pair shared with other CTAs: publish this CTA's fp32 partial of block 2p + g as
-        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes); tc_finish_kernel sums
-        // the partials in CTA order and writes the block.
+        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes). With tc_fin the pair's
+        // first CTA (c - 1, whose run ends here) adds it and writes the block: this run of the
+        // pair is this CTA's first work, so the partial is ready long before c - 1 gets there.
+        // Otherwise tc_finish_kernel sums the partials in CTA order.
         float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.slot(wk.c, pr) * 2 + g) * (TPAD / 4) * 128 + row;
 #pragma unroll
         for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        if (p.tc_fin) {
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) red_release_gpu_add(p.flags + wk.c, 1);
+        }
         continue;
+      }
+      if (tail_split) {
+        // tc_fin: the rest of this pair is CTA c + 1's first run; wait (bounded) until its
+        // eight epilogue warps have published, then add its partial
+        bool got = false;
+        if (lane == 0 && ok) {
+          const int* f = p.flags + wk.c + 1;
+          while (!(got = ld_acquire_gpu(f) >= TC_EPI_WARPS)) {
+            if (b200::globaltimer_ns() > deadline) break;
+          }
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          continue;
+        }
+        (void)ld_acquire_gpu(p.flags + wk.c + 1);          // every lane's reads follow the publish
+        const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(wk.c + 1, pr) * 2 + g) * (TPAD / 4) * 128 + row;
+        float4 v4[TPAD / 4];
+#pragma unroll
+        for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
+#pragma unroll
+        for (int j = 0; j < TPAD / 4; ++j) {
+          acc[4 * j] += v4[j].x;
+          acc[4 * j + 1] += v4[j].y;
+          acc[4 * j + 2] += v4[j].z;
+          acc[4 * j + 3] += v4[j].w;
+        }
       }
       if (real) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, st);
     }
@@ -1035,7 +1087,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
     __syncthreads();
-    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, 2 * gridDim.x);
+    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, p.tc_fin ? gridDim.x : 2 * gridDim.x);
   }
 }
 
@@ -1408,7 +1460,8 @@ int launch_m(const Params& p, cudaStream_t stream) {
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
 // [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
 // [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 block pairs split between CTAs:
-// two pairs per CTA, each two [128][64] blocks.
+// two pairs per CTA, each two [128][64] blocks | [FLAG_OFF, +FLAG_CAP) (inside the gap before
+// QT_OFF) per-CTA publish counters of those partials.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
@@ -1416,7 +1469,8 @@ constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
 constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
 constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 4LL * TC_MAX_GRID * 128 * 64 * 4;
 constexpr long long WORKSPACE_BYTES = PX_OFF + PX_CAP;
-static_assert(16 + PART_CAP <= QT_OFF, "workspace regions overlap");
+constexpr long long FLAG_OFF = 16 + PART_CAP, FLAG_CAP = TC_MAX_GRID * 4;
+static_assert(FLAG_OFF + FLAG_CAP <= QT_OFF, "workspace regions overlap");
 
 // Shared-memory plan of the tcgen05 kernel: header, row statistics, activation scales, then
 // as many pair stages (two weight tiles + one activation tile) as fit. Returns the dynamic
@@ -1502,23 +1556,32 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
   p.px = reinterpret_cast<float*>(base + PX_OFF);
+  const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
+  const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
+  if (units * grid >= (1LL << 31)) return -8;               // the kernels' work arithmetic is 32-bit
+  // Every CTA's run at least one pair long: a split pair spans exactly two CTAs, and the first
+  // of them finishes it inside the kernel. Shorter runs (small vocabulary shards) keep the
+  // finish kernel.
+  p.tc_fin = (units / grid >= KB) ? 1 : 0;
+  p.flags = reinterpret_cast<int*>(base + FLAG_OFF);
   int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,
                      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M,
-                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out);
+                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out, p.flags, p.tc_fin ? grid : 0);
   if (rc != 0) return rc;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
   static bool smem_set[HOST_MAX_DEVICES] = {};
   const int e = allow_full_smem((const void*)kern, smem_set);
   if (e != 0) return e;
   p.pdl = 1;
-  const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
-  const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
-  if (units * grid >= (1LL << 31)) return -8;               // the kernels' work arithmetic is 32-bit
   rc = launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
   if (rc != 0) return rc;
-  rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(256), 0, stream, true, p, KB);
-  if (rc != 0 || !STATS) return rc;
-  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, 2 * grid);
+  if (!p.tc_fin) {
+    rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(256), 0, stream, true, p, KB);
+    if (rc != 0) return rc;
+  }
+  if (!STATS) return 0;
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p,
+                   p.tc_fin ? grid : 2 * grid);
 }
 
 template <bool STATS>
