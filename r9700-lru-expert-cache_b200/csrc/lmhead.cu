@@ -130,12 +130,6 @@ __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
   return d;
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
 // ---- activation prologue -----------------------------------------------------------------
 //
 // FP8_QUANT: quantize x (bf16 [M, K]) per token group of 128 straight into shared memory
