@@ -9,6 +9,7 @@ librlu's C ABI:
 * ``fused_gate_mul``       -- the MoE shared expert's sigmoid(gate) * out (+ the gate GEMV fold)
 * ``fp8_hidden_quant``     -- per-token FP8 quant of MoE hidden states (fp8_quant_shared)
 * ``moe_ops``              -- moe_sum, the routed experts' outputs summed over top_k
+* ``packs``                -- persisted W4 / FP8 head packs (save, load, cached)
 * ``sharded``              -- vocab-sharded lm_head combine and expert-id-sharded LRU
 
 The kernels live in two in-tree shared libraries (librlu.so, libb200lmhead.so) built from
@@ -16,7 +17,7 @@ The kernels live in two in-tree shared libraries (librlu.so, libb200lmhead.so) b
 """
 from . import _lib  # noqa: F401
 from . import (draft_w4_lmhead, fp8_hidden_quant, fp8_target_lmhead, fused_gate_mul,  # noqa: F401
-               fused_silu_mul_quant, lru, moe_ops, sharded)
+               fused_silu_mul_quant, lru, moe_ops, packs, sharded)
 
 __all__ = ["draft_w4_lmhead", "fp8_hidden_quant", "fp8_target_lmhead", "fused_gate_mul",
-           "fused_silu_mul_quant", "lru", "moe_ops", "sharded"]
+           "fused_silu_mul_quant", "lru", "moe_ops", "packs", "sharded"]

@@ -153,9 +153,13 @@ class Fp8TargetHead:
     """Drop-in replacement for the lm_head's quant_method.apply at decode M
     (fp8_target_lmhead.py:77-93)."""
 
-    def __init__(self, orig_method, weight: torch.Tensor):
+    def __init__(self, orig_method, weight: torch.Tensor, pack_path: str | None = None):
         self.orig = orig_method
-        self.wq, self.ws = pack_fp8_block(weight)
+        if pack_path is None:
+            self.wq, self.ws = pack_fp8_block(weight)
+        else:                                   # persisted pack of this weight, else pack + save
+            from .packs import cached_fp8
+            self.wq, self.ws = cached_fp8(weight, pack_path)
         self.n_fp8 = 0
 
     def apply(self, layer, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
