@@ -92,8 +92,7 @@ struct Params {
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
   int kw;            // tcgen05 path: 128-K blocks per stage
   float* px;         // tcgen05 path: partial accumulators of blocks split along K
-  int tc_fin;        // tcgen05 path: 1 = split pairs finished inside the kernel (no finish kernel)
-  int* flags;        // tcgen05 path, tc_fin: per-CTA count of epilogue warps that published
+  int* flags;        // tcgen05 path: per-CTA count of epilogue warps that published a partial
 };
 
 // Release / acquire on a gpu-scope counter (the in-kernel finish of split tcgen05 pairs).
@@ -534,13 +533,16 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 // Work split (stream-K): a unit is one stage (block pair, 128-K block); CTA c takes the
 // contiguous units [U c / G, U (c+1) / G) of all U = ceil(nblk/2) * K/128, so no CTA does more
 // than one unit above the mean (whole blocks per CTA would run 1187 blocks on 148 SMs as 9
-// against 8, and a 149-block vocabulary shard as 2 against 1). A CTA writes its fp32 partial
-// [128 rows][T] of each block of a pair it shares with other CTAs, and per token its (max,
-// argmax, sum exp) over the blocks it finished; tc_finish_kernel (the programmatic dependent,
-// same grid) sums each shared pair's partials in CTA order and writes those blocks, and
-// stats_merge_kernel merges the row statistics. No CTA waits for another, and no fence or
-// atomic sits on the streaming path. With an odd block count the last pair's second block
-// lies beyond the tensor: the copy fills it with zeros and nothing of it is written.
+// against 8, and a 149-block vocabulary shard as 2 against 1). A pair shared by several CTAs
+// is finished by the CTA that began it: every later contributor's run of that pair is the
+// contributor's FIRST work, so it writes its fp32 partial [128 rows][T] of each block and
+// raises its publish counter (release) long before the first CTA, at the end of its own run,
+// waits for the counters (acquire, bounded), adds the partials and writes the blocks. No
+// contributor waits before it publishes and the last CTA never waits, so the chain ends. Per
+// token, each CTA leaves (max, argmax, sum exp) over the blocks it wrote, which
+// stats_merge_kernel (the programmatic dependent) merges. With an odd block count the last
+// pair's second block lies beyond the tensor: the copy fills it with zeros and nothing of it
+// is written.
 
 constexpr int TC_ISSUERS = 2;                       // MMA-issuing warps, one per block of a pair
 constexpr int TC_EPI_WARPS = 8;
@@ -876,7 +878,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint64_t deadline = b200::globaltimer_ns() + WAIT_NS;
-  griddep_launch_dependents();              // tc_finish_kernel may be scheduled as SMs free up
+  griddep_launch_dependents();              // stats_merge_kernel may be scheduled as SMs free up
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -1013,50 +1015,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
         if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
       }
-      const bool head_split = j0 != 0, tail_split = j1 != wk.KBS - 1;
-      if (head_split || (tail_split && !p.tc_fin)) {
-        // A pair shared with other CTAs: publish this CTA's fp32 partial of block 2p + g as
-        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes). With tc_fin the pair's
-        // first CTA (c - 1, whose run ends here) adds it and writes the block: this run of the
-        // pair is this CTA's first work, so the partial is ready long before c - 1 gets there.
-        // Otherwise tc_finish_kernel sums the partials in CTA order.
+      if (j0 != 0) {
+        // This CTA's run covers the middle or the end of a pair another CTA began, and it is
+        // this CTA's first work: publish the fp32 partial of block 2p + g as
+        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes), then count this warp
+        // into the CTA's publish counter (release). The pair's first CTA adds it.
         float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.slot(wk.c, pr) * 2 + g) * (TPAD / 4) * 128 + row;
 #pragma unroll
         for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        if (p.tc_fin) {
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) red_release_gpu_add(p.flags + wk.c, 1);
-        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_gpu_add(p.flags + wk.c, 1);
         continue;
       }
-      if (tail_split) {
-        // tc_fin: the rest of this pair is CTA c + 1's first run; wait (bounded) until its
-        // eight epilogue warps have published, then add its partial
-        bool got = false;
-        if (lane == 0 && ok) {
-          const int* f = p.flags + wk.c + 1;
-          while (!(got = ld_acquire_gpu(f) >= TC_EPI_WARPS)) {
-            if (b200::globaltimer_ns() > deadline) break;
+      if (j1 != wk.KBS - 1) {
+        // This CTA began the pair and its run ends inside it: the rest is the first run of each
+        // following contributor. Wait (bounded) until each one's eight epilogue warps have
+        // published, in CTA order, and add its partial; then write the block here.
+        const long long u0 = (long long)pr * wk.KBS;
+        int prev = wk.c;
+        for (int u = j1 + 1; u < wk.KBS && ok; ++u) {
+          const int cc = wk.owner(u0 + u);
+          if (cc == prev) continue;
+          prev = cc;
+          bool got = false;
+          if (lane == 0) {
+            while (!(got = ld_acquire_gpu(p.flags + cc) >= TC_EPI_WARPS)) {
+              if (b200::globaltimer_ns() > deadline) break;
+            }
+          }
+          if (!__shfl_sync(0xffffffffu, got, 0)) {
+            ok = false;
+            break;
+          }
+          (void)ld_acquire_gpu(p.flags + cc);                // every lane's reads follow the publish
+          const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(cc, pr) * 2 + g) * (TPAD / 4) * 128 + row;
+          float4 v4[TPAD / 4];
+#pragma unroll
+          for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
+#pragma unroll
+          for (int j = 0; j < TPAD / 4; ++j) {
+            acc[4 * j] += v4[j].x;
+            acc[4 * j + 1] += v4[j].y;
+            acc[4 * j + 2] += v4[j].z;
+            acc[4 * j + 3] += v4[j].w;
           }
         }
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-          ok = false;
-          continue;
-        }
-        (void)ld_acquire_gpu(p.flags + wk.c + 1);          // every lane's reads follow the publish
-        const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(wk.c + 1, pr) * 2 + g) * (TPAD / 4) * 128 + row;
-        float4 v4[TPAD / 4];
-#pragma unroll
-        for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
-#pragma unroll
-        for (int j = 0; j < TPAD / 4; ++j) {
-          acc[4 * j] += v4[j].x;
-          acc[4 * j + 1] += v4[j].y;
-          acc[4 * j + 2] += v4[j].z;
-          acc[4 * j + 3] += v4[j].w;
-        }
+        if (!ok) continue;
       }
       if (real) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, st);
     }
@@ -1081,74 +1086,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
     __syncthreads();
-    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, p.tc_fin ? gridDim.x : 2 * gridDim.x);
-  }
-}
-
-// Completes the block pairs fp8_tc_kernel split between CTAs: sums their fp32 partials in CTA
-// order, writes both blocks like the main kernel and puts the row statistics in partial slot
-// G + blockIdx.x (next to the main grid's G slots). Launched as the programmatic dependent of
-// fp8_tc_kernel with the same grid size G; 256 threads: warp w handles rows 32 (w & 3) .. + 31
-// of block 2p + (w >> 2).
-template <int TPAD, bool STATS>
-__global__ void __launch_bounds__(256) tc_finish_kernel(Params p, int KBS) {
-  __shared__ b200::RowStat red[8 * 64];
-  __shared__ float tr_all[8][TC_CHUNK * 33];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = warp >> 2, qd = warp & 3, row = 32 * qd + lane;
-  const int G = gridDim.x, nblk = p.N / 128;
-  const TcWork wk = tc_work((nblk + 1) / 2, KBS, G, 0);
-  b200::RowStat st[TPAD / TC_CHUNK];
-#pragma unroll
-  for (int i = 0; i < TPAD / TC_CHUNK; ++i) b200::rowstat_init(st[i]);
-  griddep_launch_dependents();              // stats_merge_kernel may be scheduled
-  griddep_wait();                           // the main grid has finished; its writes are visible
-  // CTA c finishes the pair in which main-grid CTA c's units start, when that start is inside
-  // a pair whose first unit belongs to CTA c - 1: every split pair has exactly one such c.
-  const int c = blockIdx.x;
-  const long long lu_c = wk.LU * c / G;
-  if (c > 0 && lu_c % KBS != 0 && wk.owner(lu_c / KBS * KBS) == c - 1) {
-    const int pr = (int)(lu_c / KBS);
-    const int blk = 2 * pr + g;
-    const long long u0 = (long long)pr * KBS;
-    float acc[TPAD];
-#pragma unroll
-    for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
-    int prev = -1;
-    for (int u = 0; u < KBS; ++u) {
-      const int cc = wk.owner(u0 + u);
-      if (cc == prev) continue;
-      prev = cc;
-      const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(cc, pr) * 2 + g) * (TPAD / 4) * 128 + row;
-      float4 v4[TPAD / 4];
-#pragma unroll
-      for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
-#pragma unroll
-      for (int j = 0; j < TPAD / 4; ++j) {
-        acc[4 * j] += v4[j].x;
-        acc[4 * j + 1] += v4[j].y;
-        acc[4 * j + 2] += v4[j].z;
-        acc[4 * j + 3] += v4[j].w;
-      }
-    }
-    if (blk < nblk) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr_all[warp], st);
-  }
-  if constexpr (STATS) {
-    for (int i = 0; i < 64; i += 32) red[warp * 64 + i + lane] = b200::RowStat{-INFINITY, 0x7fffffff, 0.f};
-    __syncwarp();
-    if (lane < TC_CHUNK) {
-#pragma unroll
-      for (int i = 0; i < TPAD / TC_CHUNK; ++i) red[warp * 64 + TC_CHUNK * i + lane] = st[i];
-    }
-    __syncthreads();
-    stats_write_partial(p, red, 64, 8, G + blockIdx.x, 2 * G);
+    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, gridDim.x);
   }
 }
 
 // Final (max, first argmax, logsumexp) of token blockIdx.x from its `nslots` partials: the max
 // and the smallest index attaining it first, then sum_i s_i exp(m_i - max) as independent terms
 // (no chain of rescalings), each in a fixed reduction order. 256 threads; the programmatic
-// dependent of tc_finish_kernel.
+// dependent of the GEMM kernel.
 __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) {
   __shared__ float s_m[8];
   __shared__ int s_i[8];
@@ -1553,14 +1498,10 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
   const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
   if (units * grid >= (1LL << 31)) return -8;               // the kernels' work arithmetic is 32-bit
-  // Every CTA's run at least one pair long: a split pair spans exactly two CTAs, and the first
-  // of them finishes it inside the kernel. Shorter runs (small vocabulary shards) keep the
-  // finish kernel.
-  p.tc_fin = (units / grid >= KB) ? 1 : 0;
   p.flags = reinterpret_cast<int*>(base + FLAG_OFF);
   int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,
                      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M,
-                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out, p.flags, p.tc_fin ? grid : 0);
+                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out, p.flags, grid);
   if (rc != 0) return rc;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
   static bool smem_set[HOST_MAX_DEVICES] = {};
@@ -1569,13 +1510,8 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   p.pdl = 1;
   rc = launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
   if (rc != 0) return rc;
-  if (!p.tc_fin) {
-    rc = launch_ex(tc_finish_kernel<TPAD, STATS>, dim3(grid), dim3(256), 0, stream, true, p, KB);
-    if (rc != 0) return rc;
-  }
   if (!STATS) return 0;
-  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p,
-                   p.tc_fin ? grid : 2 * grid);
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, grid);
 }
 
 template <bool STATS>

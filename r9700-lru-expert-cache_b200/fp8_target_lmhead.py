@@ -95,11 +95,13 @@ def _check(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor) -> None:
 
 def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset: int = 0,
                want_logits: bool = True, out: torch.Tensor | None = None,
-               debug_quant: bool = False):
+               debug_quant: bool = False, stats_out: tuple | None = None):
     """Fused quant + GEMV + row statistics.
 
     Returns (logits bf16 [M, N] | None, row_max fp32 [M], argmax int64 [M] (+ vocab_offset),
-    logsumexp fp32 [M]) and, with ``debug_quant``, the quantized activation (q, scales)."""
+    logsumexp fp32 [M]) and, with ``debug_quant``, the quantized activation (q, scales).
+    ``out`` / ``stats_out`` = (row_max, argmax, logsumexp) take caller-owned outputs (no
+    allocation per call, e.g. inside a decode loop or a CUDA graph)."""
     _check(x, wq, ws)
     M, K = x.shape
     N = wq.shape[0]
@@ -107,9 +109,16 @@ def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset
     y = None
     if want_logits:
         y = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-    mx = torch.empty(M, dtype=torch.float32, device=dev)
-    arg = torch.empty(M, dtype=torch.int64, device=dev)
-    lse = torch.empty(M, dtype=torch.float32, device=dev)
+    if stats_out is not None:
+        mx, arg, lse = stats_out
+        if (mx.dtype, arg.dtype, lse.dtype) != (torch.float32, torch.int64, torch.float32) or \
+                min(mx.numel(), arg.numel(), lse.numel()) < M:
+            raise ValueError("fp8 lm_head: stats_out must be (fp32 [M], int64 [M], fp32 [M])")
+        _lib.require_cuda("fp8 lm_head", mx, arg, lse)
+    else:
+        mx = torch.empty(M, dtype=torch.float32, device=dev)
+        arg = torch.empty(M, dtype=torch.int64, device=dev)
+        lse = torch.empty(M, dtype=torch.float32, device=dev)
     qx = torch.empty(M, K, dtype=FP8, device=dev) if debug_quant else None
     xs = torch.empty(M, K // _BLK, dtype=torch.float32, device=dev) if debug_quant else None
     wsp = workspace(dev)

@@ -52,6 +52,22 @@ def _combine(mx: torch.Tensor, ar: torch.Tensor, ls: torch.Tensor):
     return gmax.float(), arg, lse.float()
 
 
+def pack_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """(max, argmax, lse) of M rows -> one float64 [M, 3] tensor (argmax exact below 2^53) in a
+    single kernel (b200_pack_row_stats): the layout the combine exchanges, and a single
+    device-to-host copy for a caller that reads the triples on the host."""
+    from . import _lib
+    _lib.require_cuda("pack_row_stats", mx, arg, lse, out)
+    M = mx.numel()
+    arg64 = arg if arg.dtype == torch.int64 else arg.to(torch.int64)
+    if out is None:
+        out = torch.empty(M, 3, dtype=torch.float64, device=mx.device)
+    _lib.check(_lib.lmhead().b200_pack_row_stats(_lib.ptr(mx), _lib.ptr(arg64), _lib.ptr(lse), M,
+                                                 _lib.ptr(out), _lib.stream_ptr()), "b200_pack_row_stats")
+    return out
+
+
 def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, group=None):
     """All-gather this rank's per-row (max, argmax, lse) and combine: [M, 3] float64 per
     rank (24 B/row) in one collective; every rank returns the global triple. On CUDA the
