@@ -1236,23 +1236,26 @@ __global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restric
   }
   __threadfence_system();                   // this thread's peer stores, before the arrival
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int q = 0; q < world; ++q)
-      st_release_sys(reinterpret_cast<unsigned long long*>(peers[q] + data_bytes) + rank, k + 1);
+  // thread q raises this rank's arrival in peer q's buffer and waits for rank q's arrival in
+  // this rank's buffer: the world round trips overlap instead of running one after another
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int q = threadIdx.x; q < world; q += blockDim.x) {
+    st_release_sys(reinterpret_cast<unsigned long long*>(peers[q] + data_bytes) + rank, k + 1);
     const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(peers[rank] + data_bytes);
     const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
-    bool ok = true;
-    for (int q = 0; q < world && ok; ++q) {
-      uint32_t n = 0;
-      while (ld_acquire_sys(mine + q) < k + 1) {
-        if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) {
-          ok = false;
-          break;
-        }
+    uint32_t n = 0;
+    while (ld_acquire_sys(mine + q) < k + 1) {
+      if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) {
+        s_bad = 1;
+        break;
       }
     }
-    if (!ok) atomicExch(&g_lmhead_err, 2);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_bad) atomicExch(&g_lmhead_err, 2);
     *counter = k + 1;
   }
   __syncthreads();
