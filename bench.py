@@ -685,6 +685,13 @@ def main():
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     e2e_serial_ms = timed_e2e(lambda n: [serial_step(i) for i in range(n)])
 
+    # device error word of the lm_head kernels (1: a bounded pipeline wait timed out, 2: a peer
+    # never arrived at the combine), max over ranks: a timed run that tripped one is reported
+    derr = torch.tensor([float(P._lib.lmhead().b200_lmhead_error(0))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(derr, op=dist.ReduceOp.MAX)
+    device_error = int(derr.item())
+
     # ---- secondary: expert-sharded LRU on every rank, then rank-0 extras ------------------
     lru = None
     if not args.no_extras:
@@ -744,6 +751,7 @@ def main():
             "e2e_serial": {"value": total_bytes / (e2e_serial_ms * 1e-3) / 1e9, "unit": "GB/s",
                            "ms_per_step": e2e_serial_ms,
                            "mode": "the same with copy in, head, pack, copy out in series"},
+            "device_error": device_error,
             "gpu_launches": args.steps * (head_launches(n_loc) * math.ceil(M_ROWS / 64)
                                           + (0 if world == 1 else 1 if combiner else 2)),
             "combine": None if world == 1 else ("nvlink peer memory, 1 kernel" if combiner else "nccl all_gather"),
