@@ -129,6 +129,25 @@ __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Offset-binary nibbles -> (code - zero) as f16x2, exactly. nz holds f16(-(1024 + zero)) in
+// both halves, nz64 = nz + 960 = f16(-(64 + zero)). Pairs 0 and 2 (nibbles 0 and 2 of each
+// half-word): (w & 0x000F000F) | 0x6400 gives 1024 + code, plus nz. Pairs 1 and 3 are masked in
+// place (0x00F0 | 0x6400 gives 1024 + 16 code) and fma'd by 1/16 and nz64: 64 + code - 64 - zero.
+// Every value is a small integer, so each f16 operation is exact. One shift serves pairs 2, 3.
+__device__ __forceinline__ void w4_dequant_word(uint32_t w, uint32_t nz, uint32_t nz64, uint32_t (&o)[4]) {
+  const uint32_t w8 = w >> 8;
+  o[0] = hadd2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), nz);
+  o[1] = hfma2_u32(lop3_and_or(w, 0x00F000F0u, 0x64006400u), 0x2C002C00u, nz64);     // 1/16
+  o[2] = hadd2_u32(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), nz);
+  o[3] = hfma2_u32(lop3_and_or(w8, 0x00F000F0u, 0x64006400u), 0x2C002C00u, nz64);
+}
+
 // ---- activation prologue -----------------------------------------------------------------
 //
 // FP8_QUANT: quantize x (bf16 [M, K]) per token group of 128 straight into shared memory
@@ -281,7 +300,7 @@ __device__ __forceinline__ void w4_stage(const Params& p, const char* stage, con
       const unsigned short sb = *reinterpret_cast<const unsigned short*>(szbase + j * W4S_SZ_BYTES + (g + 8) * 2);
       scA = __uint_as_float((uint32_t)sa << 16);
       scB = __uint_as_float((uint32_t)sb << 16);
-      nzA = nzB = 0xE408E408u;
+      nzA = nzB = 0xE408E408u;                          // f16(-1032) twice
     } else {
       const uint32_t szA = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + g * 4);
       const uint32_t szB = *reinterpret_cast<const uint32_t*>(szbase + j * W4_SZ_BYTES + (g + 8) * 4);
@@ -291,6 +310,7 @@ __device__ __forceinline__ void w4_stage(const Params& p, const char* stage, con
       nzB = (szB >> 16) | (szB & 0xffff0000u);
     }
     const uint32_t wa[4] = {A.x, A.y, A.z, A.w}, wb[4] = {B.x, B.y, B.z, B.w};
+    const uint32_t nzA64 = hadd2_u32(nzA, 0x63806380u), nzB64 = hadd2_u32(nzB, 0x63806380u);   // + 960
     const int kb = kb0 + j;
     float acc[NT8][4];
 #pragma unroll
@@ -298,11 +318,8 @@ __device__ __forceinline__ void w4_stage(const Params& p, const char* stage, con
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       uint32_t pa[4], pb[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        pa[q] = hadd2_u32(lop3_and_or(wa[w] >> (4 * q), 0x000F000Fu, 0x64006400u), nzA);
-        pb[q] = hadd2_u32(lop3_and_or(wb[w] >> (4 * q), 0x000F000Fu, 0x64006400u), nzB);
-      }
+      w4_dequant_word(wa[w], nzA, nzA64, pa);
+      w4_dequant_word(wb[w], nzB, nzB64, pb);
 #pragma unroll
       for (int nt = 0; nt < NT8; ++nt) {
         const uint4 X = *reinterpret_cast<const uint4*>(xbase + (8 * nt + g) * p.xs_stride + (kb * 128 + 32 * w + 8 * t) * 2);
