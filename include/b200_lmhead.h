@@ -66,7 +66,7 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
                     long long workspace_bytes, cudaStream_t stream);
 
 /* b200_fp8_lmhead without the workspace argument: the scratch is a device array inside the
- * library (about 22.3 MB per device), for callers that cannot allocate device memory. No
+ * library (about 12.9 MB per device), for callers that cannot allocate device memory. No
  * counterpart in the reference. Extra codes: -9 K > 16384, -13 device index >= 64. The first
  * call per device looks the array up; one array serves all streams of a device, so calls must
  * not overlap on the GPU. */

@@ -730,42 +730,29 @@ __global__ void __launch_bounds__(128)
   if (hl == 0) sr[m * KB + kb] = sc;
 }
 
-// Units of one CTA: F whole blocks (c*F ...), then leftover units [lu0, lu1) of the blocks
-// from lb0 = G*F on. A unit is (block, stage j of KBS along K); for the tcgen05 kernel a
-// "block" is a block pair. The kernel uses F = 0 (plain stream-K), so a pair is split
-// between at most a few neighbouring CTAs.
+// Units of one CTA: the contiguous run [lu0, lu1) of all LU = npairs * KBS units (stream-K);
+// unit lu is (block pair lu / KBS, 128-K block lu % KBS). A pair shared with other CTAs is
+// begun by one CTA and continued by the next ones' FIRST runs.
 struct TcWork {
-  int F, KBS, G, c, lb0;
+  int KBS, G, c;
   long long LU, lu0, lu1;
-  __device__ int total() const { return F * KBS + (int)(lu1 - lu0); }
-  __device__ void unit(int i, int& blk, int& j) const {
-    if (i < F * KBS) {
-      blk = c * F + i / KBS;
-      j = i % KBS;
-    } else {
-      const long long lu = lu0 + (i - F * KBS);
-      blk = lb0 + (int)(lu / KBS);
-      j = (int)(lu % KBS);
-    }
+  __device__ int total() const { return (int)(lu1 - lu0); }
+  __device__ void unit(int i, int& pair, int& j) const {
+    const long long lu = lu0 + i;
+    pair = (int)(lu / KBS);
+    j = (int)(lu % KBS);
   }
-  // CTA that processes leftover unit lu (the largest c with LU*c/G <= lu). The host keeps
-  // LU * G below 2^31, so the arithmetic is 32-bit.
+  // CTA that processes unit lu (the largest c with LU*c/G <= lu). The host keeps LU * G below
+  // 2^31, so the arithmetic is 32-bit.
   __device__ int owner(long long lu) const { return (((int)lu + 1) * G - 1) / (int)LU; }
-  // Partial slot of CTA cc for leftover block b: 0 if b is the first block of cc's leftover run.
-  __device__ int slot(int cc, int b) const {
-    const int l0 = (int)LU * cc / G;
-    return (cc * 2 + ((b == lb0 + l0 / KBS) ? 0 : 1));
-  }
 };
 
-__device__ __forceinline__ TcWork tc_work(int nblk, int KBS, int G, int c) {
+__device__ __forceinline__ TcWork tc_work(int npairs, int KBS, int G, int c) {
   TcWork w;
   w.G = G;
   w.c = c;
   w.KBS = KBS;
-  w.F = 0;
-  w.lb0 = w.G * w.F;
-  w.LU = (long long)(nblk - w.lb0) * KBS;
+  w.LU = (long long)npairs * KBS;
   w.lu0 = w.LU * w.c / w.G;
   w.lu1 = w.LU * (w.c + 1) / w.G;
   return w;
@@ -1037,7 +1024,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // this CTA's first work: publish the fp32 partial of block 2p + g as
         // [T/4][128 rows][4] (each warp store one contiguous 512 bytes), then count this warp
         // into the CTA's publish counter (release). The pair's first CTA adds it.
-        float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.slot(wk.c, pr) * 2 + g) * (TPAD / 4) * 128 + row;
+        float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.c * 2 + g) * (TPAD / 4) * 128 + row;
 #pragma unroll
         for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
         __threadfence();
@@ -1066,7 +1053,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           (void)ld_acquire_gpu(p.flags + cc);                // every lane's reads follow the publish
-          const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)wk.slot(cc, pr) * 2 + g) * (TPAD / 4) * 128 + row;
+          const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)cc * 2 + g) * (TPAD / 4) * 128 + row;
           float4 v4[TPAD / 4];
 #pragma unroll
           for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
@@ -1419,14 +1406,14 @@ int launch_m(const Params& p, cudaStream_t stream) {
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
 // [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
 // [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 block pairs split between CTAs:
-// two pairs per CTA, each two [128][64] blocks | [FLAG_OFF, +FLAG_CAP) (inside the gap before
-// QT_OFF) per-CTA publish counters of those partials.
+// one pair per CTA (its first run), two [T/4][128][4] blocks | [FLAG_OFF, +FLAG_CAP) (inside
+// the gap before QT_OFF) per-CTA publish counters of those partials.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
 constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
 constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
-constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 4LL * TC_MAX_GRID * 128 * 64 * 4;
+constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 2LL * TC_MAX_GRID * 128 * 64 * 4;
 constexpr long long WORKSPACE_BYTES = PX_OFF + PX_CAP;
 constexpr long long FLAG_OFF = 16 + PART_CAP, FLAG_CAP = TC_MAX_GRID * 4;
 static_assert(FLAG_OFF + FLAG_CAP <= QT_OFF, "workspace regions overlap");
@@ -1806,7 +1793,7 @@ int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
 // b200_fp8_lmhead needs a caller-owned workspace. Some callers cannot hand one over: a plain C
 // or ctypes binding that has no device allocator of its own, or code running where an
 // allocation is not allowed (a caching allocator's hook, a memory-capped pool). For those the
-// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 22.3 MB per
+// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 12.9 MB per
 // device, reserved when the library's device code is loaded).
 
 namespace {
