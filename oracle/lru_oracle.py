@@ -199,6 +199,19 @@ def gather_expected(dst: list, src: list, slab_bytes: list, miss: np.ndarray, n_
     return dst
 
 
+def residency_audit(slot_expert, dst: list, src: list, slab_bytes: list) -> list[tuple[int, int]]:
+    """(slot, buffer) pairs whose bytes differ from the slab of the expert the slot claims:
+    the residency audit of tests/lru/test_slots_prod.py (every occupied slot, every buffer)."""
+    bad = []
+    for sl, e in enumerate(np.asarray(slot_expert).tolist()):
+        if e < 0:
+            continue
+        for i, (d, sv, b) in enumerate(zip(dst, src, slab_bytes)):
+            if not np.array_equal(np.asarray(d[sl * b:(sl + 1) * b]), np.asarray(sv[e * b:(e + 1) * b])):
+                bad.append((sl, i))
+    return bad
+
+
 def state_digest(s: LruState) -> int:
     """64-bit digest of every field the reference's tests compare after a step
     (tests/lru/test_lru.py:124-137): table, map_cold, slot_expert, slot_stamp, step,

@@ -2,7 +2,8 @@
 the CPU oracle and the reference's own numpy model (golden digests): every state field is
 compared bit-exact after EVERY step, as tests/lru/test_lru.py does; the fused kernel's align
 outputs exactly (stable in-bucket order) and against vLLM's moe_align_block_size when that
-op loads; graph replay; gather bytes from pinned host memory."""
+op loads; graph replay; gather bytes from pinned host memory; a graph of many layers replayed
+with changing routing under a residency audit of every slot."""
 from __future__ import annotations
 
 import numpy as np
@@ -249,3 +250,66 @@ def test_gather_bytes_from_pinned_host(cuda):
         for e, sl in st.miss[:nm].tolist():
             for i, b in enumerate(sizes):
                 assert torch.equal(dst[i][sl * b:(sl + 1) * b].cpu(), src[i][e * b:(e + 1) * b]), (n, e, sl, i)
+
+
+def test_graph_of_layers_replayed_with_changing_routing(cuda):
+    """tests/lru/test_graph_lru.py and test_slots_prod.py together: L layers of (manage +
+    gather) captured once and replayed 20 times with fresh Zipf routing written into the
+    captured id buffers; after every replay each layer's state equals the oracle's, the
+    table / slot invariants hold, the cache has moved, and every occupied slot's six slabs hold
+    the bytes of the expert it claims (pinned host sources, UVA gather)."""
+    L, E, S = 12, 512, 257
+    sizes = [64, 32, 16, 16, 48, 16]
+    g = torch.Generator().manual_seed(7)
+    rng = np.random.default_rng(17)
+    layers, states, srcs, dsts = [], [], [], []
+    for _ in range(L):
+        src = [torch.randint(0, 256, (E * b,), dtype=torch.uint8, generator=g).pin_memory() for b in sizes]
+        hot = sorted(rng.choice(E, S, replace=False).tolist())
+        stamps = rng.permutation(S) + 1
+        st = LO.warm_state(E, S, hot, stamps=stamps, step=S, cap=64)
+        lay = P.lru.LruLayer(**to_dev(st, 64), max_distinct=128, max_inserts=64)
+        dst = [torch.empty(S * b, dtype=torch.uint8, device=DEV) for b in sizes]
+        for d, sv, b in zip(dst, src, sizes):               # the warm set is resident
+            d.view(S, b).copy_(sv.view(E, b)[torch.as_tensor(hot)].to(DEV))
+        layers.append(lay), states.append(st), srcs.append(src), dsts.append(dst)
+    ids = [torch.zeros(50, dtype=torch.int32, device=DEV) for _ in range(L)]
+
+    def step():
+        for lay, i, d, sv in zip(layers, ids, dsts, srcs):
+            lay.manage(i)
+            lay.gather([x.view(S, b) for x, b in zip(d, sizes)], [x.view(E, b) for x, b in zip(sv, sizes)],
+                       chunks=8, lanes=16)
+    snaps = [lay.snapshot() for lay in layers]
+    dsnap = [[x.clone() for x in d] for d in dsts]          # the warm-up's gathers are undone too
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()                                               # warm-up (then restored)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    for lay, sn, d, ds in zip(layers, snaps, dsts, dsnap):
+        lay.restore(sn)
+        for x, y in zip(d, ds):
+            x.copy_(y)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    torch.cuda.synchronize()
+    for lay, sn in zip(layers, snaps):
+        lay.restore(sn)
+    first = [st.slot_expert.copy() for st in states]
+    for rep in range(20):
+        routes = [LO.zipf_rows(rng, E, 5, 10).ravel().astype(np.int32) for _ in range(L)]
+        for i, r in zip(ids, routes):
+            i.copy_(torch.as_tensor(r, device=DEV))
+        gr.replay()
+        torch.cuda.synchronize()
+        for l in range(L):
+            LO.manage(states[l], routes[l], 128, 64)
+            compare({k: getattr(layers[l], k) for k in ORDER}, states[l], f"replay {rep} layer {l}")
+            assert LO.check_invariants(states[l]) == []
+            host = [x.cpu().numpy() for x in dsts[l]]
+            assert LO.residency_audit(states[l].slot_expert, host, [x.numpy() for x in srcs[l]], sizes) == [], \
+                (rep, l)
+    assert any(not np.array_equal(f, st.slot_expert) for f, st in zip(first, states)), "cache never moved"

@@ -184,3 +184,24 @@ def test_align_sizes_formula():
     assert LO.align_sizes(50, 512, 16) == (800, 50)
     assert LO.align_sizes(200, 512, 16) == (3200, 200)
     assert LO.align_sizes(2048, 512, 16) == (2048 + 512 * 15, (2048 + 512 * 15 + 15) // 16)
+
+
+def test_residency_audit_catches_a_planted_byte():
+    """The audit of tests/lru/test_slots_prod.py, with its negative control done on the CPU:
+    a consistent cache passes, one flipped byte in one slot's slab is reported (slot, buffer)."""
+    rng = np.random.default_rng(2)
+    E, S, sizes = 64, 16, [32, 16]
+    src = [rng.integers(0, 256, E * b, dtype=np.uint8) for b in sizes]
+    hot = sorted(rng.choice(E, S, replace=False).tolist())
+    st = LO.warm_state(E, S, hot, cap=8)
+    dst = [np.zeros(S * b, dtype=np.uint8) for b in sizes]
+    for sl, e in enumerate(hot):
+        for d, sv, b in zip(dst, src, sizes):
+            d[sl * b:(sl + 1) * b] = sv[e * b:(e + 1) * b]
+    assert LO.residency_audit(st.slot_expert, dst, src, sizes) == []
+    for step in range(5):                                   # manage + gather keep it consistent
+        LO.manage(st, rng.choice(E, size=10, replace=False), 32, 8)
+        LO.gather_expected(dst, src, sizes, st.miss, st.n_miss)
+        assert LO.residency_audit(st.slot_expert, dst, src, sizes) == []
+    dst[1][5 * sizes[1] + 3] ^= 0x10                        # the planted mistake
+    assert LO.residency_audit(st.slot_expert, dst, src, sizes) == [(5, 1)]
