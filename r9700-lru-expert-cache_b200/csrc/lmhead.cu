@@ -1103,6 +1103,7 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) 
   __shared__ int s_i[8];
   __shared__ float s_s[8];
   const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_launch_dependents();              // a peer-memory combine may launch behind it
   griddep_wait();
   const float* base = p.partial + (long long)m * nslots * 3;
   float pm[2], ps[2];
@@ -1226,6 +1227,9 @@ __global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restric
   __shared__ unsigned long long s_k;
   if (threadIdx.x == 0) s_k = *counter;
   __syncthreads();
+  // launched as a programmatic dependent: the statistics are read only after the kernel that
+  // writes them (the merge) has completed
+  griddep_wait();
   const unsigned long long k = s_k;
   const long long data_bytes = 2LL * world * M_cap * 3 * 8;
   const int par = (int)(k & 1);
@@ -1700,10 +1704,9 @@ int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, c
                                unsigned long long* counter, float* out_max, long long* out_arg,
                                float* out_lse, cudaStream_t stream) {
   if (M < 0 || M > M_cap || world <= 0 || rank < 0 || rank >= world) return -1;
-  p2p_combine_kernel<<<1, 128, 0, stream>>>(row_max, row_arg, row_lse, M, M_cap,
-                                            reinterpret_cast<char* const*>(peers), rank, world, counter,
-                                            out_max, out_arg, out_lse);
-  return (int)cudaGetLastError();
+  return launch_ex(p2p_combine_kernel, dim3(1), dim3(128), 0, stream, true, row_max, row_arg, row_lse, M,
+                   M_cap, reinterpret_cast<char* const*>(peers), rank, world, counter, out_max, out_arg,
+                   out_lse);
 }
 
 // Read-only control: streams `bytes` from w with 16-byte loads over `wgs` CTAs of 256.
