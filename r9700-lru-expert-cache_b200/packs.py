@@ -75,7 +75,7 @@ def _write(path: str, kind: str, meta: dict, tensors: dict[str, torch.Tensor],
     header = json.dumps({"kind": kind, "layout": LAYOUT[kind], **meta, "source": source,
                          "tensors": entries}, sort_keys=True).encode()
     start = (len(MAGIC) + 8 + len(header) + ALIGN - 1) // ALIGN * ALIGN
-    tmp = path + ".tmp"
+    tmp = f"{path}.{os.getpid()}.tmp"           # per writer: concurrent writers never share it
     with open(tmp, "wb") as f:
         f.write(MAGIC + struct.pack("<II", VERSION, len(header)) + header)
         for e, b in zip(entries, blobs):
