@@ -731,9 +731,12 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3",
             "data": "synthetic: W ~N(0,0.02) bf16 -> pack_fp8_block, x ~N(0,1) bf16, seeded",
             "config": {"workload": "fp8_target_lmhead vocab-sharded N=151936 K=2560 M=64 "
-                                   "(fused group-128 quant + GEMV + max/argmax/logsumexp + NCCL combine)",
+                                   "(fused group-128 quant + tcgen05 block-scaled GEMM + "
+                                   "max/argmax/logsumexp; with N>1 the per-shard triples are "
+                                   "combined over NVLink peer memory)",
                        "vocab_rows_per_gpu": n_loc, "weight_pool_copies": len(pool),
-                       "l2": "weights rotated through a pool > 2.5x L2 (streamed from HBM each step)",
+                       "l2": "weight pool > 2.5x L2 (the 389 MB head alone is; streamed from HBM "
+                             "every step)",
                        "parallelism": f"vocab-sharded x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
