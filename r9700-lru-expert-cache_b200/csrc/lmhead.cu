@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   stats_write_partial(p, red, MAXM, NC, blockIdx.x, gridDim.x);
 }
 
-// ---- tcgen05 path: 16 < M <= 64 tokens ---------------------------------------------------------
+// ---- tcgen05 path: 9 <= M <= 64 tokens ----------------------------------------------------------
 //
 // At these row counts the GEMV's warp MMAs would issue-bound the SM, so the contraction moves
 // to the 5th-generation tensor core: D[128 weight rows, T tokens] (fp32, in TMEM) = W tile
