@@ -196,14 +196,11 @@ def cpu_baseline_ops() -> dict:
 # GPU pieces
 # ---------------------------------------------------------------------------------------
 
-def head_launches(n_rows: int, k: int = K_HID, sms: int = 148) -> int:
-    """Kernels of one 64-token FP8 head chunk on the tcgen05 path: activation tiles, GEMM,
-    statistics merge, plus the split-pair finish kernel when some CTA's run is shorter than a
-    block pair (the host rule in csrc/lmhead.cu: units // grid < K/128)."""
-    kb = k // 128
-    units = ((n_rows // 128 + 1) // 2) * kb
-    grid = min(units, sms, 160)
-    return 3 if units // grid >= kb else 4
+def head_launches(n_rows: int) -> int:
+    """Kernels of one 64-token FP8 head chunk on the tcgen05 path, for any shard size: the
+    activation tiles, the GEMM (split block pairs are finished inside it) and the statistics
+    merge."""
+    return 3
 
 
 def arm_config(world: int, n_loc: int) -> dict:
