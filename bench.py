@@ -550,7 +550,8 @@ def main():
     torch.manual_seed(0)
     x = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
     y = torch.empty(M_ROWS, n_loc, dtype=torch.bfloat16, device=dev)
-    # per 64-token chunk: activation tiles, tcgen05 GEMM, split-block finish, statistics merge;
+    # per 64-token chunk: activation tiles, the tcgen05 GEMM (split pairs finished inside it),
+    # the statistics merge;
     # with N > 1 one peer-memory combine (two kernels around NCCL on the fallback path)
 
     def head(i):
@@ -752,7 +753,7 @@ def main():
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                          "peak_source": pk["source"], "kernel_us": kern_us_max,
                          "kernel": "fp8_tc_kernel<64> (tcgen05); timed with its launch set "
-                                   "(act_tiles + tc (+ finish for small shards) + merge, one CUDA graph per step), "
+                                   "(act_tiles + tc + merge, one CUDA graph per step), "
                                    "so achieved is a lower bound",
                          "bytes_per_launch_set": per_launch_bytes,
                          "read_control_GB_s": ceiling},
