@@ -368,6 +368,14 @@ def ops_bench(P, dev) -> dict:
     xs = torch.randn(8, 1024, device=dev, dtype=torch.bfloat16)
     us = time_graph(lambda: P.fused_silu_mul_quant.silu_mul_quant(xs, torch.float8_e4m3fn), 200, dev)
     res["silu_mul_quant_T8_d512"] = {"us_per_call": us, "bytes": 8 * 2048 + 8 * 512 + 8 * 4}
+    vops = vllm_ops()
+    if vops is not None:                         # vLLM's silu_and_mul + scaled_fp8_quant pair
+        ic2 = torch.empty(8, 512, device=dev, dtype=torch.bfloat16)
+
+        def vpair():
+            torch.ops._C.silu_and_mul(ic2, xs)
+            vops.scaled_fp8_quant(ic2, use_per_token_if_dynamic=True)
+        res["silu_mul_quant_T8_d512"]["vllm_pair_us_per_call"] = time_graph(vpair, 200, dev)
     # large-T sweep point: [8192, 2x512] bf16 inputs rotated through a pool larger than L2
     T, d = 8192, 512
     bufs = [torch.randn(T, 2 * d, device=dev, dtype=torch.bfloat16) for _ in range(8)]
@@ -411,6 +419,10 @@ def ops_bench(P, dev) -> dict:
     xh = torch.randn(20, K_HID, device=dev, dtype=torch.bfloat16)
     res["hidden_quant_T20"] = {
         "us_per_call": time_graph(lambda: HQ.scaled_fp8_quant(xh, use_per_token_if_dynamic=True), 200, dev)}
+    vops = vllm_ops()
+    if vops is not None:                         # the library op the reference calls, same inputs
+        res["hidden_quant_T20"]["vllm_us_per_call"] = time_graph(
+            lambda: vops.scaled_fp8_quant(xh, use_per_token_if_dynamic=True), 200, dev)
     xs_big = [torch.randn(T, K_HID, device=dev, dtype=torch.bfloat16) for _ in range(4)]
     it = {"i": 0}
 
@@ -426,6 +438,8 @@ def ops_bench(P, dev) -> dict:
     ic3 = torch.randn(20, TOPK, K_HID, device=dev, dtype=torch.bfloat16)
     osum = torch.empty(20, K_HID, device=dev, dtype=torch.bfloat16)
     res["moe_sum_T20_k10"] = {"us_per_call": time_graph(lambda: MO.moe_sum(ic3, osum), 200, dev)}
+    if vops is not None:
+        res["moe_sum_T20_k10"]["vllm_us_per_call"] = time_graph(lambda: vops.moe_sum(ic3, osum), 200, dev)
     Tm = 2048
     ins = [torch.randn(Tm, TOPK, K_HID, device=dev, dtype=torch.bfloat16) for _ in range(3)]
     osum = torch.empty(Tm, K_HID, device=dev, dtype=torch.bfloat16)
@@ -438,6 +452,18 @@ def ops_bench(P, dev) -> dict:
     nb = Tm * TOPK * K_HID * 2 + Tm * K_HID * 2
     res[f"moe_sum_T{Tm}_k10"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
     return res
+
+
+def vllm_ops():
+    """vLLM's custom-op module when its compiled ops load on this GPU, else None (they are a
+    comparison only)."""
+    try:
+        from vllm import _custom_ops as ops
+        t = torch.randn(2, 64, device="cuda", dtype=torch.bfloat16)
+        ops.scaled_fp8_quant(t, use_per_token_if_dynamic=True)
+        return ops
+    except Exception:                                         # noqa: BLE001
+        return None
 
 
 def probe_ceiling(P, dev, nbytes: int) -> float:
@@ -462,7 +488,7 @@ def probe_ceiling(P, dev, nbytes: int) -> float:
 # ---------------------------------------------------------------------------------------
 
 def run_op(args):
-    """One op alone, eager launches (what ncu captures): --op fp8|w4|lru|silu."""
+    """One op alone, eager launches (what ncu captures): --op fp8|w4|lru|silu|gate|moe_sum|hquant."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     P = load_pkg()
@@ -486,6 +512,20 @@ def run_op(args):
         x = torch.randn(8, 1024, device=dev, dtype=torch.bfloat16)
         fn = lambda: P.fused_silu_mul_quant.silu_mul_quant(x, torch.float8_e4m3fn)
         nbytes = 20512
+    elif args.op == "gate":                      # --m rows of the [T, 2560] shared-expert gate
+        out = torch.randn(args.m, K_HID, device=dev, dtype=torch.bfloat16)
+        g = torch.randn(args.m, 1, device=dev, dtype=torch.bfloat16)
+        fn = lambda: P.fused_gate_mul.sigmoid_gate_mul(g, out)
+        nbytes = 2 * args.m * K_HID * 2 + args.m * 2
+    elif args.op == "moe_sum":                   # --m tokens x top-10 rows of 2560
+        x = torch.randn(args.m, TOPK, K_HID, device=dev, dtype=torch.bfloat16)
+        o = torch.empty(args.m, K_HID, device=dev, dtype=torch.bfloat16)
+        fn = lambda: P.moe_ops.moe_sum(x, o)
+        nbytes = args.m * TOPK * K_HID * 2 + args.m * K_HID * 2
+    elif args.op == "hquant":                    # --m rows of 2560 hidden-state quant
+        x = torch.randn(args.m, K_HID, device=dev, dtype=torch.bfloat16)
+        fn = lambda: P.fp8_hidden_quant.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+        nbytes = args.m * K_HID * 3 + args.m * 4
     elif args.op == "lru":
         from oracle import lru_oracle as LO
         rng = np.random.default_rng(0)
@@ -519,7 +559,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the secondary measurements")
-    ap.add_argument("--op", choices=["fp8", "w4", "lru", "silu"], default=None,
+    ap.add_argument("--op", choices=["fp8", "w4", "lru", "silu", "gate", "moe_sum", "hquant"], default=None,
                     help="time one op alone with eager launches (for profiling)")
     ap.add_argument("--m", type=int, default=M_ROWS)
     ap.add_argument("--rows", type=int, default=N_VOCAB)
