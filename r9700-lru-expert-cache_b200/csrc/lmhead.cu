@@ -617,20 +617,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int TPAD>
-__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[TPAD]) {
-  float a[32];
-  tmem_ld32(taddr, a);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = a[i];
-  if constexpr (TPAD == 64) {
-    float b[32];
-    tmem_ld32(taddr + 32, b);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[32 + i] = b[i];
-  }
-}
-
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
