@@ -313,6 +313,37 @@ def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
             "method": "52 fused launches in one CUDA graph, median over replays"}
 
 
+def lru_gather_bench(P, dev, experts: int = 128) -> dict:
+    """lru_gather from pinned host memory (UVA) into device slots: the six per-expert slabs of
+    the reference's MXFP4 MoE layer (819200 + 409600 + 51200 + 640 + 25600 + 2560 B = 1.31 MB per
+    expert, the sizes its tests use) for 1, 4, 16 and 52 missed experts; GB/s over the host link,
+    median of 5 calls each."""
+    sizes = [819200, 409600, 51200, 640, 25600, 2560]
+    g = torch.Generator().manual_seed(3)
+    srcs = [torch.randint(0, 256, (experts, b), dtype=torch.uint8, generator=g).pin_memory() for b in sizes]
+    slots = 64
+    dsts = [torch.empty(slots, b, dtype=torch.uint8, device=dev) for b in sizes]
+    res = {}
+    for n in (1, 4, 16, 52):
+        miss = torch.stack([torch.arange(n) * 2 % experts, torch.arange(n)], 1).to(torch.int32).to(dev)
+        nm = torch.tensor([n], dtype=torch.int32, device=dev)
+        torch.ops.vllm.r4d_lru_gather(dsts, srcs, miss, nm, 8, 16)
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            torch.ops.vllm.r4d_lru_gather(dsts, srcs, miss, nm, 8, 16)
+            b.record()
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b) * 1e-3)
+        t = statistics.median(ts)
+        res[f"experts_{n}"] = {"us": t * 1e6, "GB_s": n * sum(sizes) / t / 1e9}
+    ok = all(torch.equal(dsts[i][j].cpu(), srcs[i][(2 * j) % experts]) for i in range(6) for j in range(52))
+    res["bytes_checked"] = ok
+    return res
+
+
 def ops_bench(P, dev) -> dict:
     """The secondary configurations on one GPU: us/call in a CUDA graph over a pool > L2."""
     pk = peaks()["hbm_gbs"]
@@ -761,6 +792,7 @@ def main():
     ops = ceiling = None
     if rank == 0 and world == 1 and not args.no_extras:
         ops = ops_bench(P, dev)
+        ops["lru_gather_pinned_host"] = lru_gather_bench(P, dev)
         ceiling = probe_ceiling(P, dev, n_loc * K_HID)
     if world > 1:
         dist.barrier()
