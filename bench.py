@@ -774,17 +774,18 @@ def main():
     e2e_serial_ms = timed_e2e(lambda n: [serial_step(i) for i in range(n)])
 
     # The same double-buffered step captured as CUDA graphs (one per buffer parity and weight
-    # copy), the way a decode engine replays its step: in each, step i's head, pack and result
-    # copy to the host run on the compute stream while step i+1's input copy from the host runs
-    # on the copy stream, joined before the graph ends.
+    # copy), the way a decode engine replays its step: in graph i, step i's head and pack run on
+    # the compute stream while the copy stream brings step i+1's input from the host and takes
+    # step i-1's result triples back to it; the two join before the graph ends. The last
+    # step's result copy follows the loop, inside the timed region.
     def pipe_step(i):
         b, nb = i % nbuf, (i + 1) % nbuf
         cur = torch.cuda.current_stream(dev)        # the capture stream while capturing
         copy_s.wait_stream(cur)
         with torch.cuda.stream(copy_s):
             xd[nb].copy_(xh[nb], non_blocking=True)
+            res_h[nb].copy_(res_d[nb], non_blocking=True)      # step i-1's triples (parity nb)
         compute(i, b)
-        res_h[b].copy_(res_d[b], non_blocking=True)
         cur.wait_stream(copy_s)
     ngr = nbuf * len(pool)
     for i in range(ngr):                         # warm the captured path once, eagerly
@@ -801,6 +802,7 @@ def main():
         xd[0].copy_(xh[0], non_blocking=True)    # step 0's input, inside the timed region
         for i in range(n):
             egraphs[i % ngr].replay()
+        res_h[(n - 1) % nbuf].copy_(res_d[(n - 1) % nbuf], non_blocking=True)   # the last step's
     e2e_ms = timed_e2e(graph_run)
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     for gr in egraphs:                           # (may hold NCCL work: release before teardown)
