@@ -1822,8 +1822,10 @@ extern "C" {
 // b200_fp8_lmhead with the library's own scratch instead of a workspace argument; same
 // operands, outputs and return codes, plus -9 K > STATIC_SCRATCH_MAX_K and -13 device index
 // >= 64. The first call on each device looks the scratch up (make it before capturing a
-// stream). The scratch needs no clearing: every call writes what it reads. One array serves
-// every stream of a device, so calls that overlap on the GPU race on it: run them in order.
+// stream). The array keeps the previous call's bytes: the split-pair publish counters, the
+// only part that must start at zero, are zeroed by each call's first kernel, and every other
+// byte is written before it is read. One array serves every stream of a device, so calls that
+// overlap on the GPU race on it: run them in order.
 int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
                                    int N, long long vocab_offset, void* y, long long ldy,
                                    float* row_max, long long* row_arg, float* row_lse, void* qx_out,
