@@ -85,11 +85,12 @@ int b200_combine_row_stats(const double* gathered, int world, int M, float* row_
                            float* row_lse, cudaStream_t stream);
 
 /* The same combine as ONE kernel over NVLink peer memory (no NCCL call): each rank stores its
- * packed triples into every rank's peer-addressable buffer (b200_p2p_combine_bytes each; e.g.
- * torch symmetric memory), raises an arrival counter there with a system-scope release, waits
- * (bounded, 1 s; timeout sets error word 2) for all ranks and combines. `peers` is a device
- * array of the world buffer pointers as this GPU addresses them; `counter` a device uint64
- * starting at 0; buffers' counters zeroed before the first call; all ranks make the same calls. */
+ * rows, as 8-byte words carrying 32 data bits and the call's 32-bit tag, into every rank's
+ * peer-addressable buffer (b200_p2p_combine_bytes each; e.g. torch symmetric memory), reads
+ * every rank's rows from its own buffer until their tags are this call's (bounded, 1 s; timeout
+ * sets error word 2) and combines. `peers` is a device array of the world buffer pointers as
+ * this GPU addresses them; `counter` a device uint64 starting at 0; buffers zeroed before the
+ * first call; all ranks make the same calls. */
 long long b200_p2p_combine_bytes(int world, int M_cap);
 int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
                                int M_cap, void* const* peers, int rank, int world,

@@ -1185,23 +1185,31 @@ __global__ void combine_row_stats_kernel(const double* __restrict__ g, int world
 
 // ---- the same combine over NVLink peer memory, one kernel per rank ---------------------------
 // Every rank owns a buffer in memory all ranks can address (torch symmetric memory):
-// [2 parities][world][M_cap][3] float64 of packed triples, then [world] uint64 arrival counters.
-// Call k (k = this rank's device counter, equal on every rank since all make the same calls):
-// each token's thread stores the rank's triple into slot [k & 1][rank] of EVERY rank's buffer
-// (plain stores over NVLink), then thread 0 publishes arrival k + 1 into every rank's counter
-// [rank] with a system-scope release, waits -- bounded by %globaltimer -- until its own
-// counters all reach k + 1, and the block combines from its own buffer. Double-buffering by
-// parity makes reuse safe: a rank can only write parity k & 1 again at call k + 2, which needs
-// every rank's arrival k + 1, i.e. every rank has finished call k. No NCCL call, no second launch.
+// [2 parities][world source ranks][M_cap][4] uint64 words. Each word carries 32 bits of data in
+// its low half and a 32-bit call tag in its high half (the low-latency "tagged word" form of a
+// flag): a token's row is max bits, argmax low, argmax high, logsumexp bits. Call k (k = this
+// rank's device counter, equal on every rank since all make the same calls) has tag
+// (uint32)(k + 1): each token's thread stores its row, tagged, into slot [k & 1][rank] of EVERY
+// rank's buffer (8-byte relaxed system-scope stores over NVLink, each single-copy atomic), then
+// reads slot [k & 1][r] of its own buffer for every rank r, re-reading -- bounded by
+// %globaltimer -- each word whose tag is not yet this call's, and combines. A word's data and
+// tag arrive together, so no fence and no separate arrival flag sit between the stores and the
+// reads: the exchange costs one NVLink crossing. Double-buffering by parity makes reuse safe: a
+// rank writes parity k & 1 again at call k + 2 only after reading every rank's call k + 1 rows,
+// which each rank stores after it has finished call k. A tag never matches a stale word: the
+// slot last held tag k - 1 (or zero before its first use, and tags are zero only after 2^32
+// calls). No NCCL call, no second launch.
 constexpr long long P2P_WAIT_NS = 1000000000ull;
+constexpr int P2P_WORDS = 4;                // per token row: max, argmax low, argmax high, lse
+constexpr int P2P_RANK_CHUNK = 8;           // source ranks whose words one thread reads at once
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
@@ -1211,64 +1219,95 @@ __global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restric
                                                           float* __restrict__ out_mx, long long* __restrict__ out_arg,
                                                           float* __restrict__ out_lse) {
   __shared__ unsigned long long s_k;
-  if (threadIdx.x == 0) s_k = *counter;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) {
+    s_k = *counter;
+    s_bad = 0;
+  }
   __syncthreads();
   // launched as a programmatic dependent: the statistics are read only after the kernel that
   // writes them (the merge) has completed
   griddep_wait();
   const unsigned long long k = s_k;
-  const long long data_bytes = 2LL * world * M_cap * 3 * 8;
+  const unsigned long long tag = (unsigned long long)(uint32_t)(k + 1) << 32;
   const int par = (int)(k & 1);
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    const double a = (double)mx[m], b = (double)arg[m], c = (double)lse[m];
+    const unsigned long long a = (unsigned long long)arg[m];
+    const unsigned long long row[P2P_WORDS] = {
+        tag | __float_as_uint(mx[m]), tag | (a & 0xffffffffull), tag | (a >> 32), tag | __float_as_uint(lse[m])};
     for (int q = 0; q < world; ++q) {
-      double* dst = reinterpret_cast<double*>(peers[q]) + (((long long)par * world + rank) * M_cap + m) * 3;
-      dst[0] = a;
-      dst[1] = b;
-      dst[2] = c;
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[q]) +
+                                (((long long)par * world + rank) * M_cap + m) * P2P_WORDS;
+#pragma unroll
+      for (int w = 0; w < P2P_WORDS; ++w) st_relaxed_sys(dst + w, row[w]);
     }
   }
-  __threadfence_system();                   // this thread's peer stores, before the arrival
-  __syncthreads();
-  // thread q raises this rank's arrival in peer q's buffer and waits for rank q's arrival in
-  // this rank's buffer: the world round trips overlap instead of running one after another
-  __shared__ int s_bad;
-  if (threadIdx.x == 0) s_bad = 0;
-  __syncthreads();
-  for (int q = threadIdx.x; q < world; q += blockDim.x) {
-    st_release_sys(reinterpret_cast<unsigned long long*>(peers[q] + data_bytes) + rank, k + 1);
-    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(peers[rank] + data_bytes);
-    const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
+  const unsigned long long* g = reinterpret_cast<const unsigned long long*>(peers[rank]) +
+                                (long long)par * world * M_cap * P2P_WORDS;
+  const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
+  bool bad = false;
+  // Reads word `w` of rank r's row m until it carries this call's tag (bounded: `bad` ends
+  // every wait of this thread once the deadline has passed).
+  auto tagged = [&](unsigned long long v, int r, int m, int w) {
+    const unsigned long long* src = g + ((long long)r * M_cap + m) * P2P_WORDS + w;
     uint32_t n = 0;
-    while (ld_acquire_sys(mine + q) < k + 1) {
-      if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) {
-        s_bad = 1;
-        break;
+    while (!bad && (v & 0xffffffff00000000ull) != tag) {
+      if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) bad = true;
+      v = ld_relaxed_sys(src);
+    }
+    return v;
+  };
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    double gm = 0.0;
+    long long garg = 0;
+    float lse0[P2P_RANK_CHUNK];             // the first chunk's lse, kept for the sum
+    for (int r0 = 0; r0 < world; r0 += P2P_RANK_CHUNK) {
+      const int nr = min(P2P_RANK_CHUNK, world - r0);
+      unsigned long long v[P2P_RANK_CHUNK][P2P_WORDS];
+      // every word of the chunk in flight at once, then re-read the ones not yet tagged
+#pragma unroll
+      for (int i = 0; i < P2P_RANK_CHUNK; ++i)
+        if (i < nr)
+#pragma unroll
+          for (int w = 0; w < P2P_WORDS; ++w)
+            v[i][w] = ld_relaxed_sys(g + ((long long)(r0 + i) * M_cap + m) * P2P_WORDS + w);
+#pragma unroll
+      for (int i = 0; i < P2P_RANK_CHUNK; ++i) {
+        if (i >= nr) continue;
+        const int r = r0 + i;
+#pragma unroll
+        for (int w = 0; w < P2P_WORDS; ++w) v[i][w] = tagged(v[i][w], r, m, w);
+        // first rank at the global max (NaN at rank 0 stays, as in combine_row_stats_kernel)
+        const double x = (double)__uint_as_float((uint32_t)v[i][0]);
+        if (r == 0 || x > gm) {
+          gm = x;
+          garg = (long long)(((v[i][2] & 0xffffffffull) << 32) | (v[i][1] & 0xffffffffull));
+        }
+        if (r0 == 0) lse0[i] = __uint_as_float((uint32_t)v[i][3]);
       }
     }
+    double sum = 0.0;
+    for (int r = 0; r < world; ++r) {
+      float l = 0.f;
+      if (r < P2P_RANK_CHUNK) {
+#pragma unroll
+        for (int i = 0; i < P2P_RANK_CHUNK; ++i)
+          if (i == r) l = lse0[i];
+      } else {
+        const unsigned long long* src = g + ((long long)r * M_cap + m) * P2P_WORDS + 3;
+        l = __uint_as_float((uint32_t)tagged(ld_relaxed_sys(src), r, m, 3));
+      }
+      sum += exp((double)l - gm);
+    }
+    if (out_mx) out_mx[m] = (float)gm;
+    if (out_arg) out_arg[m] = garg;
+    if (out_lse) out_lse[m] = (float)(gm + log(sum));
   }
+  if (bad) s_bad = 1;
   __syncthreads();
   if (threadIdx.x == 0) {
     if (s_bad) atomicExch(&g_lmhead_err, 2);
     *counter = k + 1;
-  }
-  __syncthreads();
-  const double* g = reinterpret_cast<const double*>(peers[rank]) + (long long)par * world * M_cap * 3;
-  for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    double gm = __ldcg(g + (long long)m * 3);
-    int first = 0;
-    for (int r = 1; r < world; ++r) {
-      const double v = __ldcg(g + ((long long)r * M_cap + m) * 3);
-      if (v > gm) {
-        gm = v;
-        first = r;
-      }
-    }
-    double sum = 0.0;
-    for (int r = 0; r < world; ++r) sum += exp(__ldcg(g + ((long long)r * M_cap + m) * 3 + 2) - gm);
-    if (out_mx) out_mx[m] = (float)gm;
-    if (out_arg) out_arg[m] = (long long)__ldcg(g + ((long long)first * M_cap + m) * 3 + 1);
-    if (out_lse) out_lse[m] = (float)(gm + log(sum));
   }
 }
 
@@ -1676,14 +1715,14 @@ int b200_combine_row_stats(const double* gathered, int world, int M, float* row_
 
 // Bytes of the per-rank peer-addressable buffer b200_p2p_combine_row_stats needs.
 long long b200_p2p_combine_bytes(int world, int M_cap) {
-  return 2LL * world * M_cap * 3 * 8 + (long long)world * 8;
+  return 2LL * world * M_cap * P2P_WORDS * 8;
 }
 
 // The vocabulary-sharded combine in one kernel over NVLink peer memory (see above). `peers` is
-// a DEVICE array of `world` pointers, peers[q] = rank q's buffer as this GPU addresses it (its
-// counters zeroed before the first call); `counter` is this rank's device call counter (starts
-// at 0). Every rank must make the same sequence of calls. A peer that does not arrive within
-// 1 s sets the error word to 2 (b200_lmhead_error) and the outputs are not meaningful.
+// a DEVICE array of `world` pointers, peers[q] = rank q's buffer as this GPU addresses it
+// (zeroed before the first call); `counter` is this rank's device call counter (starts at 0).
+// Every rank must make the same sequence of calls. A peer whose rows do not arrive within 1 s
+// sets the error word to 2 (b200_lmhead_error) and the outputs are not meaningful.
 // Returns 0, -1 bad sizes, else the launch's cudaError_t.
 int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
                                int M_cap, void* const* peers, int rank, int world,

@@ -99,10 +99,11 @@ def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, gr
 
 class P2PCombiner:
     """combine_row_stats as ONE kernel over NVLink peer memory (b200_p2p_combine_row_stats):
-    each rank stores its packed (max, argmax, lse) triples straight into every rank's buffer
-    (torch symmetric memory), raises an arrival counter there, waits (bounded) for all ranks
-    and combines -- no NCCL call, no host involvement, so it can sit in a CUDA graph. Every
-    rank must make the same sequence of calls; M <= M_cap."""
+    each rank stores its (max, argmax, lse) rows straight into every rank's buffer (torch
+    symmetric memory) as 8-byte words that carry the call's tag beside 32 data bits, reads all
+    ranks' rows from its own buffer until their tags are this call's (bounded) and combines --
+    no NCCL call, no fence or arrival flag, no host involvement, so it can sit in a CUDA graph.
+    Every rank must make the same sequence of calls; M <= M_cap."""
 
     def __init__(self, M_cap: int, device: torch.device, group=None):
         import torch.distributed._symmetric_memory as symm_mem
@@ -121,7 +122,7 @@ class P2PCombiner:
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self.counter = torch.zeros(1, dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
-        dist.barrier(group)                 # every rank's counters are zero before any arrival
+        dist.barrier(group)                 # every rank's buffer is zero before any rank stores
 
     def __call__(self, mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor):
         L = self._lib
