@@ -1,9 +1,9 @@
 """The peer-memory combine kernel (b200_p2p_combine_row_stats) on one GPU, through the C ABI.
 
-world = 1: the kernel stores its rows into its own buffer and reads them back. world = 2: the
-other rank's rows are written into the buffer by the test before the call, as the tagged words
-that rank's stores leave there, so one launch runs the whole two-rank combine and no kernel
-waits on another. Both match the NCCL path's combine (b200_combine_row_stats over the float64
+world = 1: the kernel stores its rows into its own buffer and reads them back. world = 2, 8
+and 12: the other ranks' rows are written into the buffer by the test before the call, as the
+tagged words those ranks' stores leave there, so one launch runs the whole combine and no
+kernel waits on another. Both match the NCCL path's combine (b200_combine_row_stats over the float64
 triples) bit for bit, over successive calls that alternate the buffer parity and advance the
 tag. A rank whose rows never arrive, or whose rows carry a stale call's tag, makes the bounded
 wait give up after about a second with error word 2, and the context stays usable."""
@@ -92,23 +92,25 @@ def test_single_rank_round_trip(cuda, M, M_cap):
     assert lib.b200_lmhead_error(1) == 0
 
 
-@pytest.mark.parametrize("rank", [0, 1])
-def test_two_ranks_in_one_launch(cuda, rank):
-    """This rank's rows come from its own stores; the other rank's rows were placed by the test
-    with this call's tag, in the slot that rank's stores fill."""
+@pytest.mark.parametrize("world,rank", [(2, 0), (2, 1), (8, 5), (12, 3), (12, 10)])
+def test_several_ranks_in_one_launch(cuda, world, rank):
+    """This rank's rows come from its own stores; every other rank's rows were placed by the
+    test with this call's tag, in the slot that rank's stores fill. 12 ranks take the kernel's
+    second chunk of source ranks."""
     lib = L.lmhead()
-    world, M, M_cap = 2, 64, 64
+    M, M_cap = 64, 64
     _, view, peers, counter = _buffer(lib, world, M_cap, cuda)
-    other = 1 - rank
     for k in range(4):
-        mine, theirs = _stats(M, 100 + k, cuda), _stats(M, 200 + k, cuda)
+        ranks = [_stats(M, 100 * (r + 1) + k, cuda) for r in range(world)]
         if k == 2:
-            theirs[0][7] = mine[0][7]                     # equal maxima: the lower rank wins
-        view[k & 1, other, :M] = _tagged(*theirs, k + 1).to(cuda)
-        got = _call(lib, mine, M, M_cap, peers, rank, world, counter, cuda)
-        ranks = [mine, theirs] if rank == 0 else [theirs, mine]
+            for r in range(world):
+                ranks[r][0][7] = ranks[rank][0][7]        # equal maxima: the lowest rank wins
+        for r in range(world):
+            if r != rank:
+                view[k & 1, r, :M] = _tagged(*ranks[r], k + 1).to(cuda)
+        got = _call(lib, ranks[rank], M, M_cap, peers, rank, world, counter, cuda)
         _same(got, _combine_ref(lib, ranks, cuda))
-        assert torch.equal(view[k & 1, rank, :M].cpu(), _tagged(*mine, k + 1))
+        assert torch.equal(view[k & 1, rank, :M].cpu(), _tagged(*ranks[rank], k + 1))
     torch.cuda.synchronize()
     assert lib.b200_lmhead_error(1) == 0
 
