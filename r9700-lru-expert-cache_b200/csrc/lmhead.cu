@@ -1028,17 +1028,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const int cc = wk.owner(u0 + u);
           if (cc == prev) continue;
           prev = cc;
-          bool got = false;
-          if (lane == 0) {
-            while (!(got = ld_acquire_gpu(p.flags + cc) >= TC_EPI_WARPS)) {
-              if (b200::globaltimer_ns() > deadline) break;
-            }
+          // every lane polls with its own acquire load (one coalesced transaction per round),
+          // so each lane's reads of the partial follow the publish
+          bool got;
+          while (!(got = __all_sync(0xffffffffu, ld_acquire_gpu(p.flags + cc) >= TC_EPI_WARPS))) {
+            if (__any_sync(0xffffffffu, b200::globaltimer_ns() > deadline)) break;   // warp-uniform
           }
-          if (!__shfl_sync(0xffffffffu, got, 0)) {
+          if (!got) {
             ok = false;
             break;
           }
-          (void)ld_acquire_gpu(p.flags + cc);                // every lane's reads follow the publish
           const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)cc * 2 + g) * (TPAD / 4) * 128 + row;
           float4 v4[TPAD / 4];
 #pragma unroll
