@@ -126,6 +126,21 @@ def test_lmhead_entry_codes():
     assert lib.b200_silu_mul_quant(NULL, 0, 512, 1024, 0, NULL, NULL, NULL, 0, NULL) == 0
     assert lib.r4d_gemm_w4a16_nt_m64_max_m() == 64 and lib.r4d_gemm_w4a16_nt_m64_group() == 128
     assert lib.b200_lmhead_workspace_bytes() >= 16 + 148 * 16 * 12
+    # the built-in-scratch entry refuses sizes before it touches any device
+    big_k = 16384 + 128
+    assert lib.b200_fp8_lmhead_static_scratch(NULL, 1, big_k, NULL, NULL, 256, 0, NULL, 0, NULL, NULL,
+                                              NULL, NULL, NULL, NULL) == -9
+    assert lib.b200_fp8_lmhead_static_scratch(NULL, -1, 2560, NULL, NULL, 256, 0, NULL, 0, NULL, NULL,
+                                              NULL, NULL, NULL, NULL) == -1
+    assert lib.b200_fp8_lmhead_static_scratch(NULL, 0, 2560, NULL, NULL, 256, 0, NULL, 0, NULL, NULL,
+                                              NULL, NULL, NULL, NULL) == 0
+    # peer buffer of the NVLink combine: [2 parities][world][M_cap][4 tagged 8-byte words]
+    for world, m_cap in ((1, 64), (2, 64), (8, 256)):
+        assert lib.b200_p2p_combine_bytes(world, m_cap) == 2 * world * m_cap * 4 * 8
+    # bad sizes and ranks are refused before any launch
+    for M, m_cap, rank, world in ((65, 64, 0, 2), (-1, 64, 0, 2), (8, 64, 2, 2), (8, 64, 0, 0)):
+        assert lib.b200_p2p_combine_row_stats(NULL, NULL, NULL, M, m_cap, NULL, rank, world, NULL, NULL,
+                                              NULL, NULL, NULL) == -1
 
 
 def test_pick_cfg_and_legal_match_reference():
