@@ -3,9 +3,9 @@
 world = 1: the kernel stores its rows into its own buffer and reads them back. world = 2, 8
 and 12: the other ranks' rows are written into the buffer by the test before the call, as the
 tagged words those ranks' stores leave there, so one launch runs the whole combine and no
-kernel waits on another. Both match the NCCL path's combine (b200_combine_row_stats over the float64
-triples) bit for bit, over successive calls that alternate the buffer parity and advance the
-tag. A rank whose rows never arrive, or whose rows carry a stale call's tag, makes the bounded
+kernel waits on another. Both match the NCCL path's combine (b200_combine_row_stats over the
+float64 triples) bit for bit, over successive calls that alternate the buffer parity and
+advance the tag. A rank whose rows never arrive, or whose rows carry a stale call's tag, makes the bounded
 wait give up after about a second with error word 2, and the context stays usable."""
 from __future__ import annotations
 
