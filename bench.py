@@ -497,6 +497,40 @@ def vllm_ops():
         return None
 
 
+def sharded_parity(P, x, shards, rank: int, world: int, dev, combined) -> dict:
+    """Results check for N > 1, run after the timed region: every rank rebuilds the WHOLE
+    vocabulary head from the per-rank weight seeds (rank r's shard is seed 100 + r, as in
+    make_fp8_pool), runs the unsharded head on the same x and compares the combined sharded
+    (max, argmax, logsumexp) with it: argmax exact, max and logsumexp within 1e-4 (the shards
+    split the fp32 block sums between CTAs at other points, so the last bits may differ)."""
+    F8 = P.fp8_target_lmhead
+    wqs, wss = [], []
+    for r, (a, b) in enumerate(shards):
+        g = torch.Generator(device=dev).manual_seed(100 + r)
+        w = (torch.randn(b - a, K_HID, device=dev, generator=g) * 0.02).bfloat16()
+        wq, ws = F8.pack_fp8_block(w)
+        del w
+        wqs.append(wq)
+        wss.append(ws)
+    wq_full, ws_full = torch.cat(wqs), torch.cat(wss)        # strips are whole 128-row blocks
+    del wqs, wss
+    _, mx, arg, lse = F8.fp8_lmhead(x, wq_full, ws_full, want_logits=False)
+    cmx, carg, clse = combined
+    torch.cuda.synchronize(dev)
+    n_arg = int((carg != arg).sum())
+    dmax = float((cmx - mx).abs().max())
+    dlse = float((clse - lse).abs().max())
+    ok = n_arg == 0 and dmax < 1e-4 and dlse < 1e-4
+    t = torch.tensor([0.0 if ok else 1.0, float(n_arg), dmax, dlse], dtype=torch.float64, device=dev)
+    import torch.distributed as dist
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del wq_full, ws_full
+    return {"parity_ok": bool(t[0] == 0), "argmax_mismatches_max_over_ranks": int(t[1]),
+            "max_abs_dmax": float(t[2]), "max_abs_dlse": float(t[3]), "rows": int(x.shape[0]),
+            "check": "combined vocab-sharded (max, argmax, lse) vs the unsharded head on the "
+                     "same x, rebuilt on every rank; argmax exact, max/lse < 1e-4"}
+
+
 def probe_ceiling(P, dev, nbytes: int) -> float:
     """Read-only control over the same bytes (hcq_stream_probe) -> GB/s."""
     buf = torch.empty(POOL_BYTES // nbytes * nbytes + nbytes, dtype=torch.uint8, device=dev)
@@ -816,6 +850,13 @@ def main():
         dist.all_reduce(derr, op=dist.ReduceOp.MAX)
     device_error = int(derr.item())
 
+    # results check at N > 1 (outside every timed region): the combined sharded step vs the
+    # unsharded head on the same x
+    parity = None
+    if world > 1:
+        combined = [t.clone() for t in step(0)]
+        parity = sharded_parity(P, x, shards, rank, world, dev, combined)
+
     # ---- secondary: expert-sharded LRU on every rank, then rank-0 extras ------------------
     lru = None
     if not args.no_extras:
@@ -878,6 +919,7 @@ def main():
                            "ms_per_step": e2e_serial_ms,
                            "mode": "eager, with copy in, head, pack, copy out in series"},
             "device_error": device_error,
+            "parity": parity,
             "gpu_launches": args.steps * (head_launches(n_loc) * math.ceil(M_ROWS / 64)
                                           + (0 if world == 1 else 1 if combiner else 2)),
             "combine": None if world == 1 else ("nvlink peer memory, 1 kernel" if combiner else "nccl all_gather"),

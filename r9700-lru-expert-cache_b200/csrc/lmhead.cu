@@ -1720,7 +1720,8 @@ long long b200_p2p_combine_bytes(int world, int M_cap) {
 // The vocabulary-sharded combine in one kernel over NVLink peer memory (see above). `peers` is
 // a DEVICE array of `world` pointers, peers[q] = rank q's buffer as this GPU addresses it
 // (zeroed before the first call); `counter` is this rank's device call counter (starts at 0).
-// Every rank must make the same sequence of calls. A peer whose rows do not arrive within 1 s
+// Every rank must make the same sequence of calls; a call with M == 0 does nothing on any
+// rank (it launches nothing and does not count). A peer whose rows do not arrive within 1 s
 // sets the error word to 2 (b200_lmhead_error) and the outputs are not meaningful.
 // Returns 0, -1 bad sizes, else the launch's cudaError_t.
 int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
@@ -1728,6 +1729,9 @@ int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, c
                                unsigned long long* counter, float* out_max, long long* out_arg,
                                float* out_lse, cudaStream_t stream) {
   if (M < 0 || M > M_cap || world <= 0 || rank < 0 || rank >= world) return -1;
+  // no rows: no launch and no call counted (a call that exchanged nothing must not advance
+  // this rank's parity, or a later call would overwrite a slot a slower peer still reads)
+  if (M == 0) return 0;
   return launch_ex(p2p_combine_kernel, dim3(1), dim3(128), 0, stream, true, row_max, row_arg, row_lse, M,
                    M_cap, reinterpret_cast<char* const*>(peers), rank, world, counter, out_max, out_arg,
                    out_lse);
@@ -1833,21 +1837,51 @@ static_assert((long long)MAXM * STATIC_SCRATCH_MAX_K <= QR_CAP, "row region");
 
 static __device__ __align__(256) unsigned char g_static_scratch[STATIC_SCRATCH_BYTES];
 void* g_static_scratch_ptr[STATIC_SCRATCH_MAX_DEVICES] = {};
+unsigned long long g_static_scratch_ctx[STATIC_SCRATCH_MAX_DEVICES] = {};
 std::mutex g_static_scratch_mu;
 
-// Device address of this device's copy of the array, looked up on the first call made with
-// that device current. Returns 0, -13 device index beyond the table, or the CUDA error.
+// Unique id of the context current on this thread, 0 when there is none or the driver entry
+// points are unavailable. Ids are never reused within a process, so a device reset (which
+// destroys the context the array's address belongs to) shows up as a new id.
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  CUcontext ctx = nullptr;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of this device's copy of the array. It is looked up with that device
+// current (cudaGetSymbolAddress; the name itself is only a host-side stand-in) and kept
+// together with the id of the context it belongs to; a call that finds another context
+// current (after cudaDeviceReset, say) looks it up again. Returns 0, -13 device index beyond
+// the table, or the CUDA error.
 int static_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
   if (dev < 0 || dev >= STATIC_SCRATCH_MAX_DEVICES) return -13;
   std::lock_guard<std::mutex> lock(g_static_scratch_mu);
-  if (g_static_scratch_ptr[dev] == nullptr) {
+  const unsigned long long ctx = current_context_id();
+  if (g_static_scratch_ptr[dev] == nullptr || ctx == 0 || ctx != g_static_scratch_ctx[dev]) {
     void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    e = cudaGetSymbolAddress(&ptr, g_static_scratch);   // makes the primary context current
     if (e != cudaSuccess) return (int)e;
     g_static_scratch_ptr[dev] = ptr;
+    g_static_scratch_ctx[dev] = current_context_id();
   }
   *out = g_static_scratch_ptr[dev];
   return 0;
@@ -1859,8 +1893,8 @@ extern "C" {
 
 // b200_fp8_lmhead with the library's own scratch instead of a workspace argument; same
 // operands, outputs and return codes, plus -9 K > STATIC_SCRATCH_MAX_K and -13 device index
-// >= 64. The first call on each device looks the scratch up (make it before capturing a
-// stream). The array keeps the previous call's bytes: the split-pair publish counters, the
+// >= 64. The first call on each device (and the first after a device reset) looks the
+// scratch's address up, so make it before capturing a stream. The array keeps the previous call's bytes: the split-pair publish counters, the
 // only part that must start at zero, are zeroed by each call's first kernel, and every other
 // byte is written before it is read. One array serves every stream of a device, so calls that
 // overlap on the GPU race on it: run them in order.

@@ -3,8 +3,9 @@
 FP8: the fused prologue's quantized activation is bit-exact to per_token_group_quant_fp8;
 logits against the fp32 oracle ``(qx*xs) @ (wq*ws)^T`` (tests/k3/test_fp8sk.py:69,77) with
 the reference's own acceptance bound ``max|y-ref|/max|ref| < 3*3.7e-3 + 1e-4``; the fp32 row
-statistics (max within 1e-3 relative, logsumexp within 1e-3 absolute, argmax exact unless
-the oracle's top-2 gap is below 1e-3); max |dlogit| and |dlogprob| printed. W4: against
+statistics (max within 1e-5, logsumexp within 1e-4 absolute, argmax exact except on at most
+one row per call whose oracle top-2 gap is at most 1e-4, with the count printed); max
+|dlogit| and |dlogprob| printed. W4: against
 ``F.linear(x.half().float(), unpack_w4(p))`` with the reference's rel-Frobenius < 5e-3
 (tests/k3/w4_verify.py:35-56) over M in {1,2,3,5,16,20,64,129} and N=1000 padding.
 Both at the full head shape N=151936, K=2560 too. Graph replay == eager."""
@@ -33,14 +34,26 @@ def _fp8_weight(N, K, seed, dev):
     return wq, ws, Q.dequant_fp8_block(wrow, ws)
 
 
+# argmax: exact, except on rows whose oracle top-2 gap is at most ARGMAX_GAP (the kernel's
+# fp32 sums run in another order than the oracle's matmul, a few 1e-6 apart); at most
+# ARGMAX_MAX_EXEMPT such rows per call are tolerated, and their number is printed
+ARGMAX_GAP = 1e-4
+ARGMAX_MAX_EXEMPT = 1
+
+
 def _check_stats(tag, logits_ref, mx, arg, lse, offset=0):
     rmx, rarg, rlse = Q.row_stats(logits_ref)
     gap = Q.top2_gap(logits_ref)
-    assert torch.allclose(mx.cpu(), rmx.cpu(), rtol=1e-3, atol=1e-3), tag
-    assert (lse.cpu() - rlse.cpu()).abs().max().item() < 1e-3, tag
+    assert torch.allclose(mx.cpu(), rmx.cpu(), rtol=1e-5, atol=1e-5), tag
+    assert (lse.cpu() - rlse.cpu()).abs().max().item() < 1e-4, tag
+    exempt = [m for m in range(mx.numel()) if gap[m] <= ARGMAX_GAP]
     for m in range(mx.numel()):
-        if gap[m] > 1e-3:
+        if m not in exempt:
             assert int(arg[m]) == int(rarg[m]) + offset, f"{tag} row {m}"
+    print(f"{tag}: argmax exempt rows {len(exempt)}/{mx.numel()} (top-2 gap <= {ARGMAX_GAP}), "
+          f"max|dmax| {(mx.cpu() - rmx.cpu()).abs().max().item():.2e}, "
+          f"max|dlse| {(lse.cpu() - rlse.cpu()).abs().max().item():.2e}")
+    assert len(exempt) <= ARGMAX_MAX_EXEMPT, (tag, exempt)
     lp = (logits_ref.double() - rlse.double().unsqueeze(1).to(logits_ref.device))
     return lp
 

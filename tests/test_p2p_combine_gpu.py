@@ -134,3 +134,25 @@ def test_missing_or_stale_rows_time_out(cuda):
     _same(got, _combine_ref(lib, [rows, rows], cuda))
     torch.cuda.synchronize()
     assert lib.b200_lmhead_error(1) == 0 and int(counter.item()) == 3
+
+
+def test_empty_call_does_not_count(cuda):
+    """Calls with M > 0, M == 0, M > 0: the empty call launches nothing and leaves the call
+    counter alone, so the third call still uses the parity and tag that every rank expects."""
+    lib = L.lmhead()
+    world, rank, M, M_cap = 2, 0, 16, 16
+    _, view, peers, counter = _buffer(lib, world, M_cap, cuda)
+    for k, m in enumerate((M, 0, M)):
+        if m == 0:
+            rc = lib.b200_p2p_combine_row_stats(None, None, None, 0, M_cap, L.ptr(peers), rank, world,
+                                                L.ptr(counter), None, None, None, L.stream_ptr())
+            assert rc == 0
+            continue
+        call = int(counter.item())
+        ranks = [_stats(M, 300 + 10 * k + r, cuda) for r in range(world)]
+        view[call & 1, 1, :M] = _tagged(*ranks[1], call + 1).to(cuda)
+        got = _call(lib, ranks[rank], M, M_cap, peers, rank, world, counter, cuda)
+        _same(got, _combine_ref(lib, ranks, cuda))
+    torch.cuda.synchronize()
+    assert int(counter.item()) == 2
+    assert lib.b200_lmhead_error(1) == 0

@@ -80,8 +80,7 @@ def test_silu_quant_zero_row_and_empty(cuda):
     assert not FQ.supported(torch.empty(2, 2 * 16384, device=cuda, dtype=torch.bfloat16))
 
 
-def test_silu_quant_matches_vllm_pair(cuda):
-    """The reference probe's own oracle: vLLM silu_and_mul + scaled_fp8_quant (per token)."""
+def _vllm_pair_ops(cuda):
     try:
         from vllm import _custom_ops as ops
         t = torch.randn(2, 64, device=cuda, dtype=torch.bfloat16)
@@ -90,16 +89,41 @@ def test_silu_quant_matches_vllm_pair(cuda):
         ops.scaled_fp8_quant(o, use_per_token_if_dynamic=True)
     except Exception as e:  # noqa: BLE001
         pytest.skip(f"vLLM _C ops unavailable here: {type(e).__name__}")
-    for rows, d in ((1, 320), (50, 320), (2048, 320), (8, 512)):
-        x = torch.randn(rows, 2 * d, device=cuda, dtype=torch.bfloat16)
-        ic2 = torch.empty(rows, d, device=cuda, dtype=torch.bfloat16)
-        torch.ops._C.silu_and_mul(ic2, x)
-        qr, sr = ops.scaled_fp8_quant(ic2, use_per_token_if_dynamic=True)
-        act, q, s = FQ.silu_mul_quant(x, FP8, write_act=True)
-        assert _eq(act, ic2)
-        # vLLM's CUDA quant may multiply by a reciprocal; report rather than fail on q/scale
-        print(f"rows={rows} d={d}: scale equal {torch.equal(s, sr)}, "
-              f"q diffs {int((q.view(torch.uint8) != qr.view(torch.uint8)).sum())}")
+    return ops
+
+
+def test_silu_quant_matches_vllm_pair(cuda):
+    """The reference probe's own oracle, asserted as the probe asserts it
+    (tests/k4/probe_silu_quant.py:20-53): vLLM's silu_and_mul followed by
+    scaled_fp8_quant(use_per_token_if_dynamic=True) must give the same activation, the same
+    fp32 scale and the same FP8 bytes, bit for bit, over rows {1,10,50,80,2048} x d {320,640}
+    x input scale {1, 1e-3, 60} (seed 0, drawn in the probe's order) and the all-zero row,
+    whose scale is the floor 1/(448*512)."""
+    ops = _vllm_pair_ops(cuda)
+    torch.manual_seed(0)
+    bad = []
+    for rows in (1, 10, 50, 80, 2048):
+        for d in (320, 640):
+            for sc in (1.0, 1e-3, 60.0):
+                x = torch.randn(rows, 2 * d, device=cuda, dtype=torch.bfloat16) * sc
+                ic2 = torch.empty(rows, d, device=cuda, dtype=torch.bfloat16)
+                torch.ops._C.silu_and_mul(ic2, x)
+                qr, sr = ops.scaled_fp8_quant(ic2, use_per_token_if_dynamic=True)
+                act, q, s = FQ.silu_mul_quant(x, FP8, write_act=True)
+                na = int((act != ic2).sum())
+                ns = int((s.view(-1) != sr.view(-1)).sum())
+                nq = int((q.view(torch.uint8) != qr.view(torch.uint8)).sum())
+                if na or ns or nq:
+                    bad.append(f"rows={rows} d={d} x{sc}: act {na} scale {ns} q {nq}")
+    z = torch.zeros(4, 640, device=cuda, dtype=torch.bfloat16)
+    ic2 = torch.empty(4, 320, device=cuda, dtype=torch.bfloat16)
+    torch.ops._C.silu_and_mul(ic2, z)
+    qr, sr = ops.scaled_fp8_quant(ic2, use_per_token_if_dynamic=True)
+    _, q, s = FQ.silu_mul_quant(z, FP8)
+    if not (_eq(s.view(-1), sr.view(-1)) and _eq(q, qr)):
+        bad.append("zero row")
+    assert bool(s[0, 0] == torch.tensor(1.0 / (448.0 * 512.0), device=cuda))
+    assert not bad, "; ".join(bad)
 
 
 @pytest.mark.parametrize("rows,d", [(8, 512), (50, 384), (1, 128), (3, 1024)])
