@@ -656,15 +656,15 @@ def main():
     x = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
     y = torch.empty(M_ROWS, n_loc, dtype=torch.bfloat16, device=dev)
     # per 64-token chunk: activation tiles, the tcgen05 GEMM (split pairs finished inside it),
-    # the statistics merge;
-    # with N > 1 one peer-memory combine (two kernels around NCCL on the fallback path)
+    # the statistics merge -- with N > 1 the peer-memory combine runs inside the merge (two
+    # kernels around NCCL on the fallback path)
 
     def head(i):
         wq, ws = pool[i % len(pool)]
         return P.fp8_target_lmhead.fp8_lmhead(x, wq, ws, vocab_offset=r0, out=y)
 
-    # N > 1: the statistics meet over NVLink peer memory in one kernel per rank (no NCCL call
-    # on the step); NCCL's all-gather path remains as the fallback where that is unavailable.
+    # N > 1: the statistics meet over NVLink peer memory inside the head's last kernel (no NCCL
+    # call on the step); NCCL's all-gather path remains as the fallback where that is unavailable.
     combiner = None
     if world > 1:
         try:
@@ -673,9 +673,12 @@ def main():
             print(f"rank {rank}: peer-memory combine unavailable ({exc}); using NCCL", file=sys.stderr)
 
     def step(i):
+        if combiner is not None:            # the head with the peer-memory combine fused in
+            wq, ws = pool[i % len(pool)]
+            return combiner.fp8_head(x, wq, ws, r0, out=y)[1:]
         _, mx, arg, lse = head(i)
         if world > 1:
-            mx, arg, lse = combiner(mx, arg, lse) if combiner else P.sharded.combine_row_stats(mx, arg, lse)
+            mx, arg, lse = P.sharded.combine_row_stats(mx, arg, lse)
         return mx, arg, lse
 
     import torch.distributed as dist
@@ -751,10 +754,13 @@ def main():
 
     def compute(i, b):
         wq, ws = pool[i % len(pool)]
-        _, mx, arg, lse = P.fp8_target_lmhead.fp8_lmhead(xd[b], wq, ws, vocab_offset=r0, out=y,
-                                                         stats_out=st_out)
-        if world > 1:
-            mx, arg, lse = combiner(mx, arg, lse) if combiner else P.sharded.combine_row_stats(mx, arg, lse)
+        if combiner is not None:
+            _, mx, arg, lse = combiner.fp8_head(xd[b], wq, ws, r0, out=y, stats_out=st_out)
+        else:
+            _, mx, arg, lse = P.fp8_target_lmhead.fp8_lmhead(xd[b], wq, ws, vocab_offset=r0, out=y,
+                                                             stats_out=st_out)
+            if world > 1:
+                mx, arg, lse = P.sharded.combine_row_stats(mx, arg, lse)
         P.sharded.pack_row_stats(mx, arg, lse, out=res_d[b])
 
     def serial_step(i):
@@ -921,8 +927,9 @@ def main():
             "device_error": device_error,
             "parity": parity,
             "gpu_launches": args.steps * (head_launches(n_loc) * math.ceil(M_ROWS / 64)
-                                          + (0 if world == 1 else 1 if combiner else 2)),
-            "combine": None if world == 1 else ("nvlink peer memory, 1 kernel" if combiner else "nccl all_gather"),
+                                          + (0 if world == 1 or combiner else 2)),
+            "combine": None if world == 1 else (
+                "nvlink peer memory, fused into the head's statistics merge" if combiner else "nccl all_gather"),
             "clocks": clk.summary(),
             "lru": lru,
             "ops": ops,

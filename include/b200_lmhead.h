@@ -49,7 +49,9 @@ int b200_per_token_quant_fp8(const void* x, int rows, int K, long long stride_x,
  * it must not overlap on the GPU. */
 long long b200_lmhead_workspace_bytes(void);
 
-/* Device error word (1 = a bounded pipeline wait timed out); reset != 0 clears it. Synchronous. */
+/* Device error word (1 = a bounded pipeline wait timed out, 2 = a peer's statistics did not
+ * arrive at the combine); reset != 0 clears it. Synchronous. While it is set, every head call's
+ * row statistics come out poisoned (max and logsumexp NaN, argmax -1). */
 int b200_lmhead_error(int reset);
 
 /* Fused FP8 target lm_head (replaces gemm_fp8_block = per_token_group_quant_fp8 +
@@ -65,8 +67,21 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
                     float* row_lse, void* qx_out, float* xs_out, void* workspace,
                     long long workspace_bytes, cudaStream_t stream);
 
+/* b200_fp8_lmhead on this rank's vocabulary shard (vocab_offset = its first row) with the
+ * peer-memory combine of b200_p2p_combine_row_stats fused into its last kernel: row_max /
+ * row_arg / row_lse receive the GLOBAL (max, first argmax, logsumexp) over every rank's shard
+ * (the reference's all-gather + argmax over ranks, patches/models/qwen4_exp/amd/mtp.py.diff
+ * L194-227, in one launch set). peers / rank / world / counters / M_cap as for
+ * b200_p2p_combine_row_stats (M <= M_cap; the same buffer and counters may serve both).
+ * Extra code: -14 bad combine arguments. New (no single counterpart in the reference). */
+int b200_fp8_lmhead_combined(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                             long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
+                             float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                             long long workspace_bytes, void* const* peers, int rank, int world,
+                             unsigned long long* counters, int M_cap, cudaStream_t stream);
+
 /* b200_fp8_lmhead without the workspace argument: the scratch is a device array inside the
- * library (about 12.9 MB per device), for callers that cannot allocate device memory. No
+ * library (about 23.4 MB per device), for callers that cannot allocate device memory. No
  * counterpart in the reference. Extra codes: -9 K > 16384, -13 device index >= 64. The first
  * call per device looks the array up; one array serves all streams of a device, so calls must
  * not overlap on the GPU. */
@@ -89,12 +104,14 @@ int b200_combine_row_stats(const double* gathered, int world, int M, float* row_
  * peer-addressable buffer (b200_p2p_combine_bytes each; e.g. torch symmetric memory), reads
  * every rank's rows from its own buffer until their tags are this call's (bounded, 1 s; timeout
  * sets error word 2) and combines. `peers` is a device array of the world buffer pointers as
- * this GPU addresses them; `counter` a device uint64 starting at 0; buffers zeroed before the
- * first call; all ranks make the same calls. */
+ * this GPU addresses them (world <= 64); `counters` a device uint64 array [M_cap] of per-token
+ * call counters starting at 0; buffers zeroed before the first call; all ranks make the same
+ * calls with the same M (a call with M == 0 does nothing). Returns 0, -1 bad sizes, else the
+ * launch's cudaError_t. */
 long long b200_p2p_combine_bytes(int world, int M_cap);
 int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
                                int M_cap, void* const* peers, int rank, int world,
-                               unsigned long long* counter, float* out_max, long long* out_arg,
+                               unsigned long long* counters, float* out_max, long long* out_arg,
                                float* out_lse, cudaStream_t stream);
 
 /* The closed fp8hip GEMM's ABI (tests/k3/test_fp8sk.py:13-34): pre-quantized e4m3 qx [M, K]
@@ -132,6 +149,17 @@ int b200_w4_lmhead_sym(const void* x, int x_dtype, int M, int K, const void* wq,
                        int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
                        float* row_max, long long* row_arg, float* row_lse, void* workspace,
                        long long workspace_bytes, cudaStream_t stream);
+
+/* The W4 draft head on this rank's vocabulary shard with the combine fused in, as
+ * b200_fp8_lmhead_combined: sym 0 = b200_w4_lmhead's format, 1 = b200_w4_lmhead_sym's. The
+ * row outputs are the GLOBAL statistics: the sharded form of MTP.get_top_tokens /
+ * _w4_local_logits (patches/models/qwen4_exp/amd/mtp.py.diff L141-172, L194-227). Same codes
+ * as b200_w4_lmhead plus -14. */
+int b200_w4_lmhead_combined(int sym, const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+                            int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                            float* row_max, long long* row_arg, float* row_lse, void* workspace,
+                            long long workspace_bytes, void* const* peers, int rank, int world,
+                            unsigned long long* counters, int M_cap, cudaStream_t stream);
 
 /* r4d_gemm_w4a16_nt_m64 (ABI bound at kernels/draft_w4_lmhead.py:118-127): f16 a [M, K],
  * M <= 64, packed wq / wsz, bf16 c [M, N] with N = N_pad. WV/SK/MB/NPW/NT are the gfx1201

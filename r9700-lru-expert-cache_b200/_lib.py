@@ -33,6 +33,12 @@ LMHEAD_PROTOS = {
                                 c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_vp]),
     "b200_fp8_lmhead_static_scratch": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_ll, c_vp,
                                                c_ll, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "b200_fp8_lmhead_combined": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_ll, c_vp, c_ll,
+                                         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_ll,
+                                         c_vp, c_int, c_int, c_vp, c_int, c_vp]),
+    "b200_w4_lmhead_combined": (c_int, [c_int, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_int, c_ll,
+                                        c_vp, c_ll, c_vp, c_vp, c_vp, c_vp, c_ll,
+                                        c_vp, c_int, c_int, c_vp, c_int, c_vp]),
     "b200_pack_row_stats": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
     "b200_combine_row_stats": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     "b200_p2p_combine_bytes": (c_ll, [c_int, c_int]),
@@ -110,6 +116,23 @@ def stream_ptr(stream=None) -> c_vp:
 def check(rc: int, what: str) -> None:
     if rc != 0:
         raise RuntimeError(f"{what} failed rc={rc}")
+
+
+_CHECK = os.environ.get("B200_LMHEAD_CHECK", "0") == "1"
+
+
+def debug_check(what: str) -> None:
+    """With B200_LMHEAD_CHECK=1 in the environment: wait for the stream and raise if a bounded
+    device wait of the lm_head kernels ran out (the device error word). Off by default, since
+    it synchronizes; without it such a call's row statistics come out NaN / -1 instead."""
+    if not _CHECK:
+        return
+    import torch
+    torch.cuda.current_stream().synchronize()
+    err = int(lmhead().b200_lmhead_error(0))
+    if err != 0:
+        raise RuntimeError(f"{what}: device error word {err} (1: a pipeline wait ran out, "
+                           "2: a peer's statistics did not arrive); clear it with b200_lmhead_error(1)")
 
 
 def require_cuda(what: str, *tensors) -> None:

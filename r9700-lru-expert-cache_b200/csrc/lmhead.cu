@@ -92,7 +92,11 @@ struct Params {
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
   int kw;            // tcgen05 path: 128-K blocks per stage
   float* px;         // tcgen05 path: partial accumulators of blocks split along K
-  int* flags;        // tcgen05 path: per-CTA count of epilogue warps that published a partial
+  int* flags;        // tcgen05 path: split pairs' tickets and ready flags
+  // vocabulary-sharded combine fused into the statistics merge (peers == nullptr: none)
+  char* const* peers;
+  unsigned long long* counters;
+  int rank, world, M_cap, m_base;
 };
 
 // Release / acquire on a gpu-scope counter (the in-kernel finish of split tcgen05 pairs).
@@ -101,8 +105,13 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
-  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 template <int NC>
@@ -551,12 +560,12 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 // contiguous units [U c / G, U (c+1) / G) of all U = ceil(nblk/2) * K/128, so no CTA does more
 // than one unit above the mean (whole blocks per CTA would run 1187 blocks on 148 SMs as 9
 // against 8, and a 149-block vocabulary shard as 2 against 1). A pair shared by several CTAs
-// is finished by the CTA that began it: every later contributor's run of that pair is the
-// contributor's FIRST work, so it writes its fp32 partial [128 rows][T] of each block and
-// raises its publish counter (release) long before the first CTA, at the end of its own run,
-// waits for the counters (acquire, bounded), adds the partials and writes the blocks. No
-// contributor waits before it publishes and the last CTA never waits, so the chain ends. Per
-// token, each CTA leaves (max, argmax, sum exp) over the blocks it wrote, which
+// is finished by whichever of them arrives last: at the end of its run of the pair each
+// epilogue warp takes a ticket for its 32 rows; all but the last leave their fp32 partial and
+// a ready flag, and the last adds the partials in K order and writes the rows. Only the last
+// ever waits, and only for warps that took their tickets before it, which are running and
+// wait for nothing, so the kernel needs no CTA to be resident at the same time as another.
+// Per token, each CTA leaves (max, argmax, sum exp) over the blocks it wrote, which
 // stats_merge_kernel (the programmatic dependent) merges. With an odd block count the last
 // pair's second block lies beyond the tensor: the copy fills it with zeros and nothing of it
 // is written.
@@ -570,12 +579,30 @@ constexpr int TC_TILE_W = 128 * 128;
 constexpr int TC_PAIR_W = 2 * TC_TILE_W;
 constexpr int TC_HDR = 512;                         // barriers, TMEM slot
 constexpr int TC_MAX_GRID = 160;                    // partial-accumulator slots are sized for it
+// Split-pair bookkeeping in the workspace's flag region (ints, zeroed by act_tiles_kernel on
+// every call): a ticket per (pair's first CTA, block of the pair), then a ready flag per (CTA,
+// its first or last pair, block, 32-row quarter).
+constexpr int TC_TICKET_OFF = 0;
+constexpr int TC_READY_OFF = TC_MAX_GRID * 2;
+constexpr int TC_FLAG_INTS = TC_READY_OFF + TC_MAX_GRID * 2 * 2 * 4;
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Named barrier of the four epilogue warps of group g (ids 2 and 3; 0 is __syncthreads).
+__device__ __forceinline__ void group_bar(int g) {
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
+}
+
+// Does CTA c begin a block pair that continues in later CTAs (its last pair, split)? Then the
+// pair's blocks have statistics slots of their own (see fp8_tc_kernel).
+__host__ __device__ __forceinline__ bool tc_begins_split(long long LU, int G, int KBS, int c, int& pair) {
+  const long long lu0 = LU * c / G, lu1 = LU * (c + 1) / G;
+  pair = (int)((lu1 - 1) / KBS);
+  return (lu1 % KBS) != 0 && lu0 <= (long long)pair * KBS;
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
@@ -639,8 +666,9 @@ __global__ void __launch_bounds__(128)
                      uint8_t* __restrict__ qt, float* __restrict__ xt, uint8_t* __restrict__ qx_out,
                      float* __restrict__ xs_out, int* __restrict__ flags, int nflags) {
   griddep_launch_dependents();              // the GEMM may start streaming weights now
-  // the GEMM's publish counters start every call at zero (this kernel is stream-ordered after
-  // the previous call, and the GEMM touches them only after griddepcontrol.wait)
+  // the GEMM's split-pair tickets and ready flags start every call at zero (this kernel is
+  // stream-ordered after the previous call, and the GEMM touches them only after
+  // griddepcontrol.wait)
   if (blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0;
   const int KB = K / 128, kb = blockIdx.x;
@@ -840,6 +868,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* xs_bar = a_empty + TC_MAX_BUF;
   uint64_t* done_bar = xs_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  int* s_ticket = reinterpret_cast<int*>(tmem_slot + 2);       // [2 groups][2 parities]
   float* xs_s = reinterpret_cast<float*>(sm + p.xs_off);       // [KB][TPAD]
   char* ring = sm + p.ring_off;
   b200::RowStat st[TPAD / TC_CHUNK];        // epilogue lanes l < 16: tokens 16 ch + l
@@ -962,6 +991,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
     for (int i = 0; i < TPAD / TC_CHUNK; ++i) b200::rowstat_init(st[i]);
     bool ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xs_bar, 0, deadline));
+    int nsplit = 0;                           // split pairs met so far (ticket buffer parity)
     for (int it = 0; it < total;) {
       int pr, j0;
       wk.unit(it, pr, j0);
@@ -1005,54 +1035,114 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
         if (lane == 0) b200::mbar_arrive(&a_empty[buf]);
       }
-      if (j0 != 0) {
-        // This CTA's run covers the middle or the end of a pair another CTA began, and it is
-        // this CTA's first work: publish the fp32 partial of block 2p + g as
-        // [T/4][128 rows][4] (each warp store one contiguous 512 bytes), then count this warp
-        // into the CTA's publish counter (release). The pair's first CTA adds it.
-        float4* dst = reinterpret_cast<float4*>(p.px) + ((long long)wk.c * 2 + g) * (TPAD / 4) * 128 + row;
-#pragma unroll
-        for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) red_release_gpu_add(p.flags + wk.c, 1);
-        continue;
-      }
-      if (j1 != wk.KBS - 1) {
-        // This CTA began the pair and its run ends inside it: the rest is the first run of each
-        // following contributor. Wait (bounded) until each one's eight epilogue warps have
-        // published, in CTA order, and add its partial; then write the block here.
+      if ((j0 != 0 || j1 != wk.KBS - 1) && real) {
+        // The pair is split between CTAs (contiguous ones, c_first .. c_first + nseg - 1, each
+        // covering one run of its 128-K blocks). Each block's group of four warps takes a
+        // ticket; the group that arrives LAST finishes the block and the others leave their
+        // fp32 partials (one per warp, with a ready flag). A group therefore waits only for
+        // partials whose writers hold an earlier ticket, i.e. are already running and have
+        // nothing left to wait for: no CTA depends on a CTA that has not started. The block is
+        // the sum of the segments' partials in segment (K) order whoever finishes it, and its
+        // per-token statistics go to a slot of the pair's own (not to the finishing CTA's), so
+        // every output is independent of the arrival order.
         const long long u0 = (long long)pr * wk.KBS;
-        int prev = wk.c;
-        for (int u = j1 + 1; u < wk.KBS && ok; ++u) {
-          const int cc = wk.owner(u0 + u);
-          if (cc == prev) continue;
-          prev = cc;
-          // every lane polls with its own acquire load (one coalesced transaction per round),
-          // so each lane's reads of the partial follow the publish
-          bool got;
-          while (!(got = __all_sync(0xffffffffu, ld_acquire_gpu(p.flags + cc) >= TC_EPI_WARPS))) {
-            if (__any_sync(0xffffffffu, b200::globaltimer_ns() > deadline)) break;   // warp-uniform
+        const int c_first = wk.owner(u0);
+        const int nseg = wk.owner(u0 + wk.KBS - 1) - c_first + 1, me = wk.c - c_first;
+        if ((ew & 3) == 0 && lane == 0)
+          s_ticket[2 * g + (nsplit & 1)] = ok ? atom_add_acq_rel_gpu(p.flags + TC_TICKET_OFF + c_first * 2 + g, 1) : -1;
+        group_bar(g);
+        const int t = s_ticket[2 * g + (nsplit & 1)];
+        ++nsplit;
+        if (t < 0) continue;                // a wait of this group ran out earlier
+        float4* px4 = reinterpret_cast<float4*>(p.px);
+        // partial slot of segment `s`: [T/4][128 rows][4] (each warp access one contiguous 512 B)
+        auto slot = [&](int s) {
+          const int cc = c_first + s;
+          const int which = ((int)((wk.LU * cc / wk.G) / wk.KBS) == pr) ? 0 : 1;   // CTA cc's first pair?
+          return (((long long)cc * 2 + which) * 2 + g) * 4 + qd;
+        };
+        auto publish = [&](long long sl) {
+          float4* dst = px4 + (sl >> 2) * (TPAD / 4) * 128 + row;
+#pragma unroll
+          for (int j = 0; j < TPAD; j += 4) dst[(j >> 2) * 128] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        };
+        if (t < nseg - 1) {
+          const long long sl = slot(me);
+          publish(sl);
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) st_release_gpu(p.flags + TC_READY_OFF + sl, 1);
+          continue;
+        }
+        // Last: sum the segments in order. Segment 0 + this one is order-free (addition
+        // commutes); from the third segment on, this warp's own partial joins the others in
+        // memory so that the prefix is summed first.
+        if (me >= 2) publish(slot(me));
+        for (int s = 0; s < nseg && ok; ++s) {
+          if (s == me && me < 2) continue;
+          const long long sl = slot(s);
+          if (s != me) {
+            // every lane polls with its own acquire load, so each lane's reads follow the publish
+            bool got;
+            while (!(got = __all_sync(0xffffffffu, ld_acquire_gpu(p.flags + TC_READY_OFF + sl) != 0))) {
+              if (__any_sync(0xffffffffu, b200::globaltimer_ns() > deadline)) break;   // warp-uniform
+            }
+            if (!got) {
+              ok = false;
+              break;
+            }
           }
-          if (!got) {
-            ok = false;
-            break;
-          }
-          const float4* src = reinterpret_cast<const float4*>(p.px) + ((long long)cc * 2 + g) * (TPAD / 4) * 128 + row;
+          const float4* src = px4 + (sl >> 2) * (TPAD / 4) * 128 + row;
           float4 v4[TPAD / 4];
 #pragma unroll
           for (int j = 0; j < TPAD / 4; ++j) v4[j] = __ldcg(src + j * 128);
+          const bool first = (me >= 2) && (s == 0);
 #pragma unroll
           for (int j = 0; j < TPAD / 4; ++j) {
-            acc[4 * j] += v4[j].x;
-            acc[4 * j + 1] += v4[j].y;
-            acc[4 * j + 2] += v4[j].z;
-            acc[4 * j + 3] += v4[j].w;
+            acc[4 * j] = first ? v4[j].x : acc[4 * j] + v4[j].x;
+            acc[4 * j + 1] = first ? v4[j].y : acc[4 * j + 1] + v4[j].y;
+            acc[4 * j + 2] = first ? v4[j].z : acc[4 * j + 2] + v4[j].z;
+            acc[4 * j + 3] = first ? v4[j].w : acc[4 * j + 3] + v4[j].w;
           }
         }
-        if (!ok) continue;
+        // the block's rows, then its per-token statistics: each warp's (lanes < 16 hold tokens
+        // 16 ch + lane) into its transpose tile, merged over the group's four warps in a fixed
+        // order into the pair's slot G + 2 c_first + g
+        b200::RowStat bs[TPAD / TC_CHUNK];
+#pragma unroll
+        for (int i = 0; i < TPAD / TC_CHUNK; ++i) b200::rowstat_init(bs[i]);
+        if (ok) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, bs);
+        if (STATS) {
+          if (lane < TC_CHUNK) {
+#pragma unroll
+            for (int i = 0; i < TPAD / TC_CHUNK; ++i) {
+              float* e = tr + (TC_CHUNK * i + lane) * 3;
+              e[0] = bs[i].m;
+              e[1] = __int_as_float(bs[i].idx);
+              e[2] = bs[i].s;
+            }
+          }
+          group_bar(g);
+          if ((ew & 3) == 0) {
+            const float* tg = reinterpret_cast<const float*>(sm + p.x_off) + (4 * g) * (TC_CHUNK * 33);
+            for (int tk = lane; tk < p.M; tk += 32) {
+              b200::RowStat r;
+              b200::rowstat_init(r);
+              for (int w = 0; w < 4; ++w) {
+                const float* e = tg + w * (TC_CHUNK * 33) + tk * 3;
+                r = b200::rowstat_merge(r, b200::RowStat{e[0], __float_as_int(e[1]), e[2]});
+              }
+              float* dst = p.partial + ((long long)tk * 3 * wk.G + wk.G + 2 * c_first + g) * 3;
+              dst[0] = r.m;
+              dst[1] = __int_as_float(r.idx);
+              dst[2] = r.s;
+            }
+          }
+          group_bar(g);                     // the tiles are free again
+        }
+        continue;
       }
-      if (real) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, st);
+      if (real && ok) tc_block_rows<TPAD, STATS>(p, acc, blk * 128 + 32 * qd, lane, tr, st);
     }
     if (!ok) atomicExch(&g_lmhead_err, 1);
   }
@@ -1075,33 +1165,174 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
     __syncthreads();
-    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, gridDim.x);
+    stats_write_partial(p, red, 64, TC_EPI_WARPS, blockIdx.x, 3 * gridDim.x);
   }
+}
+
+// ---- vocabulary-sharded combine over NVLink peer memory ----------------------------------------
+// Every rank owns a buffer in memory all ranks can address (torch symmetric memory):
+// [2 parities][world source ranks][M_cap][4] uint64 words. Each word carries 32 bits of data in
+// its low half and a 32-bit call tag in its high half (the low-latency "tagged word" form of a
+// flag): a token's row is max bits, argmax low, argmax high, logsumexp bits. Every token m has
+// its own call counter k = counters[m] (equal on every rank, since all make the same calls),
+// and its call k has tag (uint32)(k + 1): the token's warp stores its row, tagged, into slot
+// [k & 1][rank][m] of EVERY rank's buffer (8-byte relaxed system-scope stores over NVLink,
+// each single-copy atomic), then reads slot [k & 1][r][m] of its own buffer for every rank r,
+// re-reading -- bounded by %globaltimer -- each word whose tag is not yet this call's, and
+// combines. A word's data and tag arrive together, so no fence and no separate arrival flag
+// sit between the stores and the reads: the exchange costs one NVLink crossing. Tokens are
+// independent of each other, so every token's exchange runs in its own warp. Double-buffering
+// by parity makes reuse safe: a rank writes token m's parity k & 1 again at call k + 2 only
+// after reading every rank's call k + 1 row of m, which each rank stores after it has
+// finished call k of m. A tag never matches a stale word: the slot last held tag k - 1 (or
+// zero before its first use, and tags are zero only after 2^32 calls).
+constexpr long long P2P_WAIT_NS = 1000000000ull;
+constexpr int P2P_WORDS = 4;                // per token row: max, argmax low, argmax high, lse
+constexpr int P2P_MAX_WORLD = 64;
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Token m's exchange and combine, run by one whole warp. (mx, arg, lse) is this rank's row; `w`
+// is the warp's shared scratch for the world ranks' words. The global result: the max over
+// ranks, the argmax of the first rank attaining it (shards are in vocabulary order, so the first
+// global index), logsumexp = max + log sum_r exp(lse_r - max) in float64; a NaN max at any rank
+// (a rank whose bounded wait ran out) makes max and logsumexp NaN and the argmax -1, as in
+// combine_row_stats_kernel, and so does a rank whose row did not arrive in time. Lane 0 writes the outputs (each nullable) and advances the
+// token's counter. Returns false when some rank's row did not arrive within the limit.
+__device__ bool p2p_token(float mx, long long arg, float lse, int m, int M_cap, char* const* peers, int rank,
+                          int world, unsigned long long* counters, float* out_mx, long long* out_arg,
+                          float* out_lse, unsigned long long (*w)[P2P_WORDS]) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long k = 0;
+  if (lane == 0) k = counters[m];
+  k = __shfl_sync(0xffffffffu, k, 0);
+  const uint32_t tag32 = (uint32_t)(k + 1);
+  const unsigned long long tag = (unsigned long long)tag32 << 32;
+  const int par = (int)(k & 1);
+  const unsigned long long a = (unsigned long long)arg;
+  const unsigned long long row[P2P_WORDS] = {tag | __float_as_uint(mx), tag | (a & 0xffffffffull), tag | (a >> 32),
+                                             tag | __float_as_uint(lse)};
+  for (int q = lane; q < world; q += 32) {
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[q]) +
+                              (((long long)par * world + rank) * M_cap + m) * P2P_WORDS;
+#pragma unroll
+    for (int i = 0; i < P2P_WORDS; ++i) st_relaxed_sys(dst + i, row[i]);
+  }
+  const unsigned long long* g = reinterpret_cast<const unsigned long long*>(peers[rank]) +
+                                (long long)par * world * M_cap * P2P_WORDS;
+  const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
+  bool bad = false;
+  for (int r = lane; r < world; r += 32) {
+    const unsigned long long* src = g + ((long long)r * M_cap + m) * P2P_WORDS;
+    unsigned long long v[P2P_WORDS];
+#pragma unroll
+    for (int i = 0; i < P2P_WORDS; ++i) v[i] = ld_relaxed_sys(src + i);     // all four in flight
+#pragma unroll
+    for (int i = 0; i < P2P_WORDS; ++i) {
+      uint32_t n = 0;
+      while (!bad && (uint32_t)(v[i] >> 32) != tag32) {
+        if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) bad = true;
+        v[i] = ld_relaxed_sys(src + i);
+      }
+      w[r][i] = v[i];
+    }
+  }
+  bad = __any_sync(0xffffffffu, bad);
+  __syncwarp();
+  if (lane == 0) {
+    double gm = 0.0;
+    long long garg = 0;
+    bool nan = false;
+    for (int r = 0; r < world; ++r) {
+      const double x = (double)__uint_as_float((uint32_t)w[r][0]);
+      nan = nan || (x != x);
+      if (r == 0 || x > gm) {
+        gm = x;
+        garg = (long long)(((w[r][2] & 0xffffffffull) << 32) | (w[r][1] & 0xffffffffull));
+      }
+    }
+    if (nan || bad) {                       // a rank's statistics are poisoned or missing
+      gm = __longlong_as_double(0x7ff8000000000000ll);
+      garg = -1;
+    }
+    double sum = 0.0;
+    for (int r = 0; r < world; ++r) sum += exp((double)__uint_as_float((uint32_t)w[r][3]) - gm);
+    if (out_mx) out_mx[m] = (float)gm;
+    if (out_arg) out_arg[m] = garg;
+    if (out_lse) out_lse[m] = (float)(gm + log(sum));
+    counters[m] = k + 1;
+  }
+  __syncwarp();                             // `w` is free again for the warp's next token
+  return !bad;
+}
+
+// The combine alone (the statistics come from an earlier kernel), launched as a programmatic
+// dependent, so the statistics are read only after the kernel that writes them has completed.
+// Warp w of the grid takes tokens w, w + W, w + 2W, ... in that order on every rank, so the
+// row a warp waits for is stored by the same warp of the peer after the peer's previous token,
+// whose row this warp has already stored; the grid (at most P2P_MAX_CTAS CTAs) is resident at
+// once, so every warp makes progress.
+constexpr int P2P_MAX_CTAS = 128;
+__global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
+                                                          const float* __restrict__ lse, int M, int M_cap,
+                                                          char* const* __restrict__ peers, int rank, int world,
+                                                          unsigned long long* __restrict__ counters,
+                                                          float* __restrict__ out_mx, long long* __restrict__ out_arg,
+                                                          float* __restrict__ out_lse) {
+  __shared__ unsigned long long s_w[4][P2P_MAX_WORLD][P2P_WORDS];
+  griddep_wait();
+  const int warp = threadIdx.x >> 5;
+  bool ok = true;
+  for (int m = blockIdx.x * 4 + warp; m < M; m += gridDim.x * 4)      // whole warps
+    ok = p2p_token(mx[m], arg[m], lse[m], m, M_cap, peers, rank, world, counters, out_mx, out_arg, out_lse,
+                   s_w[warp]) && ok;
+  if (!ok && (threadIdx.x & 31) == 0) atomicExch(&g_lmhead_err, 2);
 }
 
 // Final (max, first argmax, logsumexp) of token blockIdx.x from its `nslots` partials: the max
 // and the smallest index attaining it first, then sum_i s_i exp(m_i - max) as independent terms
 // (no chain of rescalings), each in a fixed reduction order. 256 threads; the programmatic
 // dependent of the GEMM kernel.
-__global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) {
+// With g_cta > 0 (the tcgen05 path) slots [0, g_cta) are the GEMM CTAs' and slots
+// g_cta + 2c + g the blocks of the split pair CTA c begins (valid only where it begins one).
+__global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots, int g_cta) {
   __shared__ float s_m[8];
   __shared__ int s_i[8];
   __shared__ float s_s[8];
+  __shared__ long long s_arg;
+  __shared__ unsigned long long s_w[P2P_MAX_WORLD][P2P_WORDS];
   const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   griddep_launch_dependents();              // a peer-memory combine may launch behind it
   griddep_wait();
   const float* base = p.partial + (long long)m * nslots * 3;
+  const int KBS = p.K / 128, nblk = p.N / 128;
+  const long long LU = (long long)((nblk + 1) / 2) * KBS;
+  auto valid = [&](int i) {
+    if (i >= nslots) return false;
+    if (g_cta <= 0 || i < g_cta) return true;
+    int pair;
+    const int j = i - g_cta;
+    return tc_begins_split(LU, g_cta, KBS, j >> 1, pair) && 2 * pair + (j & 1) < nblk;
+  };
   float pm[2], ps[2];
   int pi[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int i = threadIdx.x + 256 * k;
-    const bool v = i < nslots;
+    const bool v = valid(i);
     pm[k] = v ? __ldcg(base + 3 * i) : -INFINITY;
     pi[k] = v ? __float_as_int(__ldcg(base + 3 * i + 1)) : 0x7fffffff;
     ps[k] = v ? __ldcg(base + 3 * i + 2) : 0.f;
   }
   for (int i = threadIdx.x + 512; i < nslots; i += 256) {      // more than 512 slots: fold in
+    if (!valid(i)) continue;
     const float mm = __ldcg(base + 3 * i), ss = __ldcg(base + 3 * i + 2);
     const int ii = __float_as_int(__ldcg(base + 3 * i + 1));
     b200::RowStat a{pm[1], pi[1], ps[1]}, b{mm, ii, ss};
@@ -1142,17 +1373,43 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots) 
       t += s_s[w];
       best = min(best, s_i[w]);
     }
-    if (p.row_max) p.row_max[m] = mx;
-    if (p.row_arg) p.row_arg[m] = best;
-    if (p.row_lse) p.row_lse[m] = mx + logf(t);
+    float lse = mx + logf(t);
+    long long arg = best;
+    // A pipeline wait that ran out (this call or an earlier one not yet cleared with
+    // b200_lmhead_error(1)) leaves some blocks unwritten: the statistics say so instead of
+    // carrying a plausible value (max and logsumexp NaN, argmax -1).
+    if (*reinterpret_cast<volatile int*>(&g_lmhead_err) != 0) {
+      mx = __int_as_float(0x7fffffff);
+      lse = mx;
+      arg = -1;
+    }
+    if (p.peers == nullptr) {
+      if (p.row_max) p.row_max[m] = mx;
+      if (p.row_arg) p.row_arg[m] = arg;
+      if (p.row_lse) p.row_lse[m] = lse;
+    } else {
+      s_m[0] = mx;
+      s_s[0] = lse;
+      s_arg = arg;
+    }
   }
+  if (p.peers == nullptr) return;
+  // vocabulary-sharded: this token's row meets every rank's over peer memory (warp 0)
+  __syncthreads();
+  if (warp == 0 &&
+      !p2p_token(s_m[0], s_arg, s_s[0], p.m_base + m, p.M_cap, p.peers, p.rank, p.world, p.counters,
+                 p.row_max ? p.row_max - p.m_base : nullptr, p.row_arg ? p.row_arg - p.m_base : nullptr,
+                 p.row_lse ? p.row_lse - p.m_base : nullptr, s_w) &&
+      lane == 0)
+    atomicExch(&g_lmhead_err, 2);
 }
 
 // ---- vocabulary-sharded combine of the row statistics ---------------------------------------
 // Each rank's (max, argmax, logsumexp) per token is packed as three float64 (exact for the
 // index), all-gathered by NCCL, and combined: global max; argmax of the first rank attaining
 // it (shards are in vocabulary order, so this is the first global index); logsumexp =
-// max + log sum_r exp(lse_r - max).
+// max + log sum_r exp(lse_r - max). A NaN max at any rank (its statistics poisoned by a wait
+// that ran out) gives NaN max and logsumexp and argmax -1.
 __global__ void pack_row_stats_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
                                       const float* __restrict__ lse, int M, double* __restrict__ out) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1168,146 +1425,21 @@ __global__ void combine_row_stats_kernel(const double* __restrict__ g, int world
   if (m >= M) return;
   double gm = g[3 * m];
   int first = 0;
+  bool nan = gm != gm;
   for (int r = 1; r < world; ++r) {
     const double v = g[((long long)r * M + m) * 3];
+    nan = nan || (v != v);
     if (v > gm) {
       gm = v;
       first = r;
     }
   }
+  if (nan) gm = __longlong_as_double(0x7ff8000000000000ll);     // poisoned at some rank
   double s = 0.0;
   for (int r = 0; r < world; ++r) s += exp(g[((long long)r * M + m) * 3 + 2] - gm);
   if (mx) mx[m] = (float)gm;
-  if (arg) arg[m] = (long long)g[((long long)first * M + m) * 3 + 1];
+  if (arg) arg[m] = nan ? -1 : (long long)g[((long long)first * M + m) * 3 + 1];
   if (lse) lse[m] = (float)(gm + log(s));
-}
-
-// ---- the same combine over NVLink peer memory, one kernel per rank ---------------------------
-// Every rank owns a buffer in memory all ranks can address (torch symmetric memory):
-// [2 parities][world source ranks][M_cap][4] uint64 words. Each word carries 32 bits of data in
-// its low half and a 32-bit call tag in its high half (the low-latency "tagged word" form of a
-// flag): a token's row is max bits, argmax low, argmax high, logsumexp bits. Call k (k = this
-// rank's device counter, equal on every rank since all make the same calls) has tag
-// (uint32)(k + 1): each token's thread stores its row, tagged, into slot [k & 1][rank] of EVERY
-// rank's buffer (8-byte relaxed system-scope stores over NVLink, each single-copy atomic), then
-// reads slot [k & 1][r] of its own buffer for every rank r, re-reading -- bounded by
-// %globaltimer -- each word whose tag is not yet this call's, and combines. A word's data and
-// tag arrive together, so no fence and no separate arrival flag sit between the stores and the
-// reads: the exchange costs one NVLink crossing. Double-buffering by parity makes reuse safe: a
-// rank writes parity k & 1 again at call k + 2 only after reading every rank's call k + 1 rows,
-// which each rank stores after it has finished call k. A tag never matches a stale word: the
-// slot last held tag k - 1 (or zero before its first use, and tags are zero only after 2^32
-// calls). No NCCL call, no second launch.
-constexpr long long P2P_WAIT_NS = 1000000000ull;
-constexpr int P2P_WORDS = 4;                // per token row: max, argmax low, argmax high, lse
-constexpr int P2P_RANK_CHUNK = 8;           // source ranks whose words one thread reads at once
-
-__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restrict__ mx, const long long* __restrict__ arg,
-                                                          const float* __restrict__ lse, int M, int M_cap,
-                                                          char* const* __restrict__ peers, int rank, int world,
-                                                          unsigned long long* __restrict__ counter,
-                                                          float* __restrict__ out_mx, long long* __restrict__ out_arg,
-                                                          float* __restrict__ out_lse) {
-  __shared__ unsigned long long s_k;
-  __shared__ int s_bad;
-  if (threadIdx.x == 0) {
-    s_k = *counter;
-    s_bad = 0;
-  }
-  __syncthreads();
-  // launched as a programmatic dependent: the statistics are read only after the kernel that
-  // writes them (the merge) has completed
-  griddep_wait();
-  const unsigned long long k = s_k;
-  const unsigned long long tag = (unsigned long long)(uint32_t)(k + 1) << 32;
-  const int par = (int)(k & 1);
-  for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    const unsigned long long a = (unsigned long long)arg[m];
-    const unsigned long long row[P2P_WORDS] = {
-        tag | __float_as_uint(mx[m]), tag | (a & 0xffffffffull), tag | (a >> 32), tag | __float_as_uint(lse[m])};
-    for (int q = 0; q < world; ++q) {
-      unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[q]) +
-                                (((long long)par * world + rank) * M_cap + m) * P2P_WORDS;
-#pragma unroll
-      for (int w = 0; w < P2P_WORDS; ++w) st_relaxed_sys(dst + w, row[w]);
-    }
-  }
-  const unsigned long long* g = reinterpret_cast<const unsigned long long*>(peers[rank]) +
-                                (long long)par * world * M_cap * P2P_WORDS;
-  const uint64_t deadline = b200::globaltimer_ns() + P2P_WAIT_NS;
-  bool bad = false;
-  // Reads word `w` of rank r's row m until it carries this call's tag (bounded: `bad` ends
-  // every wait of this thread once the deadline has passed).
-  auto tagged = [&](unsigned long long v, int r, int m, int w) {
-    const unsigned long long* src = g + ((long long)r * M_cap + m) * P2P_WORDS + w;
-    uint32_t n = 0;
-    while (!bad && (v & 0xffffffff00000000ull) != tag) {
-      if ((++n & 63u) == 0 && b200::globaltimer_ns() > deadline) bad = true;
-      v = ld_relaxed_sys(src);
-    }
-    return v;
-  };
-  for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    double gm = 0.0;
-    long long garg = 0;
-    float lse0[P2P_RANK_CHUNK];             // the first chunk's lse, kept for the sum
-    for (int r0 = 0; r0 < world; r0 += P2P_RANK_CHUNK) {
-      const int nr = min(P2P_RANK_CHUNK, world - r0);
-      unsigned long long v[P2P_RANK_CHUNK][P2P_WORDS];
-      // every word of the chunk in flight at once, then re-read the ones not yet tagged
-#pragma unroll
-      for (int i = 0; i < P2P_RANK_CHUNK; ++i)
-        if (i < nr)
-#pragma unroll
-          for (int w = 0; w < P2P_WORDS; ++w)
-            v[i][w] = ld_relaxed_sys(g + ((long long)(r0 + i) * M_cap + m) * P2P_WORDS + w);
-#pragma unroll
-      for (int i = 0; i < P2P_RANK_CHUNK; ++i) {
-        if (i >= nr) continue;
-        const int r = r0 + i;
-#pragma unroll
-        for (int w = 0; w < P2P_WORDS; ++w) v[i][w] = tagged(v[i][w], r, m, w);
-        // first rank at the global max (NaN at rank 0 stays, as in combine_row_stats_kernel)
-        const double x = (double)__uint_as_float((uint32_t)v[i][0]);
-        if (r == 0 || x > gm) {
-          gm = x;
-          garg = (long long)(((v[i][2] & 0xffffffffull) << 32) | (v[i][1] & 0xffffffffull));
-        }
-        if (r0 == 0) lse0[i] = __uint_as_float((uint32_t)v[i][3]);
-      }
-    }
-    double sum = 0.0;
-    for (int r = 0; r < world; ++r) {
-      float l = 0.f;
-      if (r < P2P_RANK_CHUNK) {
-#pragma unroll
-        for (int i = 0; i < P2P_RANK_CHUNK; ++i)
-          if (i == r) l = lse0[i];
-      } else {
-        const unsigned long long* src = g + ((long long)r * M_cap + m) * P2P_WORDS + 3;
-        l = __uint_as_float((uint32_t)tagged(ld_relaxed_sys(src), r, m, 3));
-      }
-      sum += exp((double)l - gm);
-    }
-    if (out_mx) out_mx[m] = (float)gm;
-    if (out_arg) out_arg[m] = garg;
-    if (out_lse) out_lse[m] = (float)(gm + log(sum));
-  }
-  if (bad) s_bad = 1;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    if (s_bad) atomicExch(&g_lmhead_err, 2);
-    *counter = k + 1;
-  }
 }
 
 // ---- read-only stream control (hcq_stream_probe, hcq_fp8skinny.hip:206-224) -----------------
@@ -1422,7 +1554,7 @@ int launch_one(Params p, cudaStream_t stream) {
   const int grid = min(p.N / 16, num_sms());
   const int rc = launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
   if (rc != 0 || !STATS) return rc;
-  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, grid);
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, grid, 0);
 }
 
 template <int KIND, bool STATS>
@@ -1434,17 +1566,18 @@ int launch_m(const Params& p, cudaStream_t stream) {
 // [QT_OFF, +QT_CAP) swizzled activation tiles (tcgen05) | [XT_OFF, +XT_CAP) their scales |
 // [QR_OFF, +QR_CAP) quantized activation rows (GEMV) | [SR_OFF, +SR_CAP) their scales |
 // [PX_OFF, +PX_CAP) fp32 partial accumulators of the tcgen05 block pairs split between CTAs:
-// one pair per CTA (its first run), two [T/4][128][4] blocks | [FLAG_OFF, +FLAG_CAP) (inside
-// the gap before QT_OFF) per-CTA publish counters of those partials.
+// per CTA its first and its last pair, two [T/4][128][4] blocks each | [FLAG_OFF, +FLAG_CAP)
+// (inside the gap before QT_OFF) the split pairs' tickets and ready flags.
 constexpr long long PART_CAP = 1024LL * 64 * 12;
 constexpr long long QT_OFF = 1 << 20, QT_CAP = 1 << 20;
 constexpr long long XT_OFF = 2 << 20, XT_CAP = 64 << 10;
 constexpr long long QR_OFF = XT_OFF + XT_CAP, QR_CAP = 256 << 10;
 constexpr long long SR_OFF = QR_OFF + QR_CAP, SR_CAP = 16 << 10;
-constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 2LL * TC_MAX_GRID * 128 * 64 * 4;
+constexpr long long PX_OFF = SR_OFF + SR_CAP, PX_CAP = 4LL * TC_MAX_GRID * 128 * 64 * 4;
 constexpr long long WORKSPACE_BYTES = PX_OFF + PX_CAP;
-constexpr long long FLAG_OFF = 16 + PART_CAP, FLAG_CAP = TC_MAX_GRID * 4;
+constexpr long long FLAG_OFF = 16 + PART_CAP, FLAG_CAP = TC_FLAG_INTS * 4;
 static_assert(FLAG_OFF + FLAG_CAP <= QT_OFF, "workspace regions overlap");
+static_assert(3LL * TC_MAX_GRID * 64 * 12 <= PART_CAP, "statistics slots: CTAs + split pairs' blocks");
 
 // Shared-memory plan of the tcgen05 kernel: header, row statistics, activation scales, then
 // as many pair stages (two weight tiles + one activation tile) as fit. Returns the dynamic
@@ -1536,7 +1669,7 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   p.flags = reinterpret_cast<int*>(base + FLAG_OFF);
   int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,
                      static_cast<const __nv_bfloat16*>(qx_in ? nullptr : p.x), qx_in, xs_in, p.M,
-                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out, p.flags, grid);
+                     p.K, TPAD, qt, xt, p.qx_out, p.xs_out, p.flags, TC_FLAG_INTS);
   if (rc != 0) return rc;
   auto kern = fp8_tc_kernel<TPAD, STATS>;
   static bool smem_set[HOST_MAX_DEVICES] = {};
@@ -1546,7 +1679,7 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   rc = launch_ex(kern, dim3(grid), dim3(TC_THREADS), smem, stream, true, wmap, p, qt, xt);
   if (rc != 0) return rc;
   if (!STATS) return 0;
-  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, grid);
+  return launch_ex(stats_merge_kernel, dim3(p.M), dim3(256), 0, stream, true, p, 3 * grid, grid);
 }
 
 template <bool STATS>
@@ -1564,7 +1697,7 @@ constexpr int TC_MIN_M = 9;
 template <int KIND>
 int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
   const int M = p.M, KB = p.K / 128;
-  const bool stats = (p.row_max || p.row_arg || p.row_lse);
+  const bool stats = (p.row_max || p.row_arg || p.row_lse || p.peers);
   const bool is_fp8 = (KIND == FP8_QUANT || KIND == FP8_PREQ);
   const bool have_ws = p.ws != nullptr;
   const bool tc_ok = is_fp8 && have_ws && (long long)KB * 64 * 128 <= QT_CAP;
@@ -1580,6 +1713,7 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
     if (p.row_lse) q.row_lse = p.row_lse + m0;
     if (p.qx_out) q.qx_out = p.qx_out + (long long)m0 * p.K;
     if (p.xs_out) q.xs_out = p.xs_out + (long long)m0 * KB;
+    q.m_base = p.m_base + m0;
     int rc;
     if (tc_ok && q.M >= TC_MIN_M) {
       const uint8_t* qx_in = (KIND == FP8_PREQ) ? static_cast<const uint8_t*>(q.x) : nullptr;
@@ -1608,6 +1742,24 @@ int run_chunks(Params p, int x_elem_bytes, cudaStream_t stream) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// The peer-memory combine fused into a head's statistics merge (peers == nullptr: none).
+struct Combine {
+  void* const* peers = nullptr;
+  unsigned long long* counters = nullptr;
+  int rank = 0, world = 1, M_cap = 0;
+  bool valid(int M) const {
+    return M <= M_cap && world >= 1 && world <= P2P_MAX_WORLD && rank >= 0 && rank < world;
+  }
+  void apply(Params& p) const {
+    p.peers = reinterpret_cast<char* const*>(peers);
+    p.counters = counters;
+    p.rank = rank;
+    p.world = world;
+    p.M_cap = M_cap;
+    p.m_base = 0;
+  }
+};
+
 }  // namespace
 
 extern "C" {
@@ -1635,18 +1787,20 @@ int b200_lmhead_error(int reset) {
 // the quantized activation. wq / ws in the B200 packed layout (see the file header).
 // Returns 0, -1 bad M, -2 N % 128, -3 K % 128, -8 does not fit shared memory, -9 workspace
 // too small / missing when stats are asked for, -10 misaligned pointer, else a CUDA error.
-int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
-                    long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
-                    float* row_lse, void* qx_out, float* xs_out, void* workspace,
-                    long long workspace_bytes, cudaStream_t stream) {
+static int fp8_lmhead_impl(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                           long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
+                           float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                           long long workspace_bytes, const Combine& cb, cudaStream_t stream) {
   if (M < 0) return -1;
   if (N <= 0 || N % 128) return -2;
   if (K <= 0 || K % 128) return -3;
+  if (cb.peers != nullptr && !cb.valid(M)) return -14;
   if (M == 0) return 0;
-  const bool stats = row_max || row_arg || row_lse;
+  const bool stats = row_max || row_arg || row_lse || cb.peers != nullptr;
   if (stats && (workspace == nullptr || workspace_bytes < WORKSPACE_BYTES)) return -9;
   if (!aligned16(x) || !aligned16(wq) || (qx_out && !aligned16(qx_out))) return -10;
   Params p{};
+  cb.apply(p);
   p.x = x; p.M = M; p.K = K; p.N = N; p.n_valid = N; p.vocab_offset = vocab_offset;
   p.w = static_cast<const uint8_t*>(wq); p.wscale = ws;
   p.y = static_cast<__nv_bfloat16*>(y); p.ldy = ldy > 0 ? ldy : N;
@@ -1655,6 +1809,29 @@ int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws
   p.ws = static_cast<char*>(workspace);
   p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 16);
   return run_chunks<FP8_QUANT>(p, 2, stream);
+}
+
+int b200_fp8_lmhead(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                    long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
+                    float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                    long long workspace_bytes, cudaStream_t stream) {
+  return fp8_lmhead_impl(x, M, K, wq, ws, N, vocab_offset, y, ldy, row_max, row_arg, row_lse, qx_out, xs_out,
+                         workspace, workspace_bytes, Combine{}, stream);
+}
+
+// b200_fp8_lmhead on this rank's vocabulary shard with the combine of the per-token statistics
+// over NVLink peer memory fused into its last kernel (the b200_p2p_combine_row_stats exchange
+// and its `peers` / `counters` / M_cap, M <= M_cap): row_max / row_arg / row_lse receive the
+// GLOBAL (max, first argmax, logsumexp) over all ranks' shards. Logits, when asked for, are
+// this shard's. Same returns as b200_fp8_lmhead, plus -14 bad combine arguments.
+int b200_fp8_lmhead_combined(const void* x, int M, int K, const void* wq, const float* ws, int N,
+                             long long vocab_offset, void* y, long long ldy, float* row_max, long long* row_arg,
+                             float* row_lse, void* qx_out, float* xs_out, void* workspace,
+                             long long workspace_bytes, void* const* peers, int rank, int world,
+                             unsigned long long* counters, int M_cap, cudaStream_t stream) {
+  if (peers == nullptr || counters == nullptr) return -14;
+  return fp8_lmhead_impl(x, M, K, wq, ws, N, vocab_offset, y, ldy, row_max, row_arg, row_lse, qx_out, xs_out,
+                         workspace, workspace_bytes, Combine{peers, counters, rank, world, M_cap}, stream);
 }
 
 // fp8hip_gemm_w8a8_launch(qx, w, xs, ws, y, M, N, K, stream) -- the closed fp8hip GEMM's ABI
@@ -1712,28 +1889,30 @@ int b200_combine_row_stats(const double* gathered, int world, int M, float* row_
   return (int)cudaGetLastError();
 }
 
-// Bytes of the per-rank peer-addressable buffer b200_p2p_combine_row_stats needs.
+// Bytes of the per-rank peer-addressable buffer b200_p2p_combine_row_stats and the combined
+// heads need.
 long long b200_p2p_combine_bytes(int world, int M_cap) {
   return 2LL * world * M_cap * P2P_WORDS * 8;
 }
 
 // The vocabulary-sharded combine in one kernel over NVLink peer memory (see above). `peers` is
 // a DEVICE array of `world` pointers, peers[q] = rank q's buffer as this GPU addresses it
-// (zeroed before the first call); `counter` is this rank's device call counter (starts at 0).
-// Every rank must make the same sequence of calls; a call with M == 0 does nothing on any
-// rank (it launches nothing and does not count). A peer whose rows do not arrive within 1 s
-// sets the error word to 2 (b200_lmhead_error) and the outputs are not meaningful.
-// Returns 0, -1 bad sizes, else the launch's cudaError_t.
+// (zeroed before the first call); `counters` is this rank's DEVICE array of M_cap per-token
+// call counters (zeroed before the first call, shared with the combined heads below). Every
+// rank must make the same sequence of calls with the same M; a call with M == 0 does nothing.
+// A peer whose row of a token does not arrive within 1 s sets the error word to 2
+// (b200_lmhead_error) and that token's outputs are not meaningful.
+// Returns 0, -1 bad sizes (M > M_cap, world outside 1..64, rank outside the world), else the
+// launch's cudaError_t.
 int b200_p2p_combine_row_stats(const float* row_max, const long long* row_arg, const float* row_lse, int M,
                                int M_cap, void* const* peers, int rank, int world,
-                               unsigned long long* counter, float* out_max, long long* out_arg,
+                               unsigned long long* counters, float* out_max, long long* out_arg,
                                float* out_lse, cudaStream_t stream) {
-  if (M < 0 || M > M_cap || world <= 0 || rank < 0 || rank >= world) return -1;
-  // no rows: no launch and no call counted (a call that exchanged nothing must not advance
-  // this rank's parity, or a later call would overwrite a slot a slower peer still reads)
+  if (M < 0 || M > M_cap || world <= 0 || world > P2P_MAX_WORLD || rank < 0 || rank >= world) return -1;
   if (M == 0) return 0;
-  return launch_ex(p2p_combine_kernel, dim3(1), dim3(128), 0, stream, true, row_max, row_arg, row_lse, M,
-                   M_cap, reinterpret_cast<char* const*>(peers), rank, world, counter, out_max, out_arg,
+  return launch_ex(p2p_combine_kernel, dim3(std::min((M + 3) / 4, P2P_MAX_CTAS)), dim3(128), 0, stream, true,
+                   row_max, row_arg, row_lse,
+                   M, M_cap, reinterpret_cast<char* const*>(peers), rank, world, counters, out_max, out_arg,
                    out_lse);
 }
 
@@ -1754,16 +1933,18 @@ int hcq_stream_probe(void* w, long long bytes, int wgs, void* out, void* stream)
 static int w4_lmhead_impl(bool sym, const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
                    int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
                    float* row_max, long long* row_arg, float* row_lse, void* workspace,
-                   long long workspace_bytes, cudaStream_t stream) {
+                   long long workspace_bytes, const Combine& cb, cudaStream_t stream) {
   if (M < 0) return -1;
   if (N_pad <= 0 || N_pad % 16) return -2;
   if (K <= 0 || K % 128) return -3;
   if (x_dtype != 0 && x_dtype != 1) return -11;
+  if (cb.peers != nullptr && !cb.valid(M)) return -14;
   if (M == 0) return 0;
-  const bool stats = row_max || row_arg || row_lse;
+  const bool stats = row_max || row_arg || row_lse || cb.peers != nullptr;
   if (stats && (workspace == nullptr || workspace_bytes < WORKSPACE_BYTES)) return -9;
   if (!aligned16(x) || !aligned16(wq) || !aligned16(wsz)) return -10;
   Params p{};
+  cb.apply(p);
   p.x = x; p.M = M; p.K = K; p.N = N_pad;
   p.n_valid = (n_valid > 0 && n_valid < N_pad) ? n_valid : N_pad;
   p.vocab_offset = vocab_offset;
@@ -1781,7 +1962,21 @@ int b200_w4_lmhead(const void* x, int x_dtype, int M, int K, const void* wq, con
                    float* row_max, long long* row_arg, float* row_lse, void* workspace,
                    long long workspace_bytes, cudaStream_t stream) {
   return w4_lmhead_impl(false, x, x_dtype, M, K, wq, wsz, N_pad, n_valid, vocab_offset, y, ldy, row_max,
-                        row_arg, row_lse, workspace, workspace_bytes, stream);
+                        row_arg, row_lse, workspace, workspace_bytes, Combine{}, stream);
+}
+
+// b200_w4_lmhead (sym = 0) or b200_w4_lmhead_sym (sym = 1) on this rank's vocabulary shard with
+// the peer-memory combine of the statistics fused in, as b200_fp8_lmhead_combined: the row
+// outputs are the GLOBAL (max, first argmax, logsumexp). Returns as those, plus -14.
+int b200_w4_lmhead_combined(int sym, const void* x, int x_dtype, int M, int K, const void* wq, const void* wsz,
+                            int N_pad, int n_valid, long long vocab_offset, void* y, long long ldy,
+                            float* row_max, long long* row_arg, float* row_lse, void* workspace,
+                            long long workspace_bytes, void* const* peers, int rank, int world,
+                            unsigned long long* counters, int M_cap, cudaStream_t stream) {
+  if (peers == nullptr || counters == nullptr) return -14;
+  return w4_lmhead_impl(sym != 0, x, x_dtype, M, K, wq, wsz, N_pad, n_valid, vocab_offset, y, ldy, row_max,
+                        row_arg, row_lse, workspace, workspace_bytes, Combine{peers, counters, rank, world, M_cap},
+                        stream);
 }
 
 // The same head for the symmetric format: `wscale` holds bf16 scales [N_pad/16, K/128, 16]
@@ -1791,7 +1986,7 @@ int b200_w4_lmhead_sym(const void* x, int x_dtype, int M, int K, const void* wq,
                        float* row_max, long long* row_arg, float* row_lse, void* workspace,
                        long long workspace_bytes, cudaStream_t stream) {
   return w4_lmhead_impl(true, x, x_dtype, M, K, wq, wscale, N_pad, n_valid, vocab_offset, y, ldy, row_max,
-                        row_arg, row_lse, workspace, workspace_bytes, stream);
+                        row_arg, row_lse, workspace, workspace_bytes, Combine{}, stream);
 }
 
 static int g_w4_last_rc = 0;
@@ -1824,7 +2019,7 @@ int r4d_gemm_w4a16_nt_m64_group(void) { return 128; }
 // b200_fp8_lmhead needs a caller-owned workspace. Some callers cannot hand one over: a plain C
 // or ctypes binding that has no device allocator of its own, or code running where an
 // allocation is not allowed (a caching allocator's hook, a memory-capped pool). For those the
-// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 12.9 MB per
+// scratch lives in one file-scope device array of STATIC_SCRATCH_BYTES (about 23.4 MB per
 // device, reserved when the library's device code is loaded).
 
 namespace {
@@ -1894,10 +2089,11 @@ extern "C" {
 // b200_fp8_lmhead with the library's own scratch instead of a workspace argument; same
 // operands, outputs and return codes, plus -9 K > STATIC_SCRATCH_MAX_K and -13 device index
 // >= 64. The first call on each device (and the first after a device reset) looks the
-// scratch's address up, so make it before capturing a stream. The array keeps the previous call's bytes: the split-pair publish counters, the
-// only part that must start at zero, are zeroed by each call's first kernel, and every other
-// byte is written before it is read. One array serves every stream of a device, so calls that
-// overlap on the GPU race on it: run them in order.
+// scratch's address up, so make it before capturing a stream. The array keeps the previous
+// call's bytes: the split-pair tickets and ready flags, the only part that must start at zero,
+// are zeroed by each call's first kernel, and every other byte is written before it is read.
+// One array serves every stream of a device, so calls that overlap on the GPU race on it: run
+// them in order.
 int b200_fp8_lmhead_static_scratch(const void* x, int M, int K, const void* wq, const float* ws,
                                    int N, long long vocab_offset, void* y, long long ldy,
                                    float* row_max, long long* row_arg, float* row_lse, void* qx_out,

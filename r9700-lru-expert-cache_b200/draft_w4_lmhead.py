@@ -322,6 +322,7 @@ def _run(x: torch.Tensor, wq: torch.Tensor, wsz: torch.Tensor, n: int, k: int,
             n_pad, n, int(vocab_offset), _lib.ptr(y), y.stride(0), _lib.ptr(mx), _lib.ptr(arg),
             _lib.ptr(lse), _lib.ptr(wsp), 0 if wsp is None else wsp.numel(), _lib.stream_ptr())
     _lib.check(rc, "b200_w4_lmhead_sym" if sym else "b200_w4_lmhead")
+    _lib.debug_check("b200_w4_lmhead")
     return y, mx, arg, lse
 
 

@@ -127,6 +127,7 @@ def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset
         N if y is None else y.stride(0), _lib.ptr(mx), _lib.ptr(arg), _lib.ptr(lse),
         _lib.ptr(qx), _lib.ptr(xs), _lib.ptr(wsp), wsp.numel(), _lib.stream_ptr())
     _lib.check(rc, "b200_fp8_lmhead")
+    _lib.debug_check("b200_fp8_lmhead")
     res = (y, mx, arg, lse)
     return res + (qx, xs) if debug_quant else res
 

@@ -45,9 +45,10 @@ def combine_row_stats_local(parts):
 
 
 def _combine(mx: torch.Tensor, ar: torch.Tensor, ls: torch.Tensor):
-    gmax, _ = mx.max(dim=0)
+    gmax, _ = mx.max(dim=0)                  # NaN at any rank -> NaN (a poisoned shard)
     first = (mx == gmax.unsqueeze(0)).to(torch.int8).argmax(dim=0)     # first rank at gmax
     arg = ar.gather(0, first.unsqueeze(0)).squeeze(0)
+    arg = torch.where(torch.isnan(gmax), torch.full_like(arg, -1), arg)
     lse = gmax + torch.log(torch.exp(ls - gmax.unsqueeze(0)).sum(dim=0))
     return gmax.float(), arg, lse.float()
 
@@ -98,12 +99,19 @@ def combine_row_stats(mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor, gr
 
 
 class P2PCombiner:
-    """combine_row_stats as ONE kernel over NVLink peer memory (b200_p2p_combine_row_stats):
-    each rank stores its (max, argmax, lse) rows straight into every rank's buffer (torch
-    symmetric memory) as 8-byte words that carry the call's tag beside 32 data bits, reads all
-    ranks' rows from its own buffer until their tags are this call's (bounded) and combines --
-    no NCCL call, no fence or arrival flag, no host involvement, so it can sit in a CUDA graph.
-    Every rank must make the same sequence of calls; M <= M_cap."""
+    """combine_row_stats over NVLink peer memory, with no NCCL call and no host involvement, so
+    it can sit in a CUDA graph. Each rank stores its (max, argmax, lse) rows straight into every
+    rank's buffer (torch symmetric memory) as 8-byte words that carry the call's tag beside 32
+    data bits, reads all ranks' rows from its own buffer until their tags are this call's
+    (bounded) and combines; every token has its own call counter.
+
+    * ``__call__(mx, arg, lse)``: the combine alone, one kernel (b200_p2p_combine_row_stats).
+    * ``fp8_head(x, wq, ws, vocab_offset)`` / ``w4_head(x, packed, vocab_offset)``: this
+      rank's head on its vocabulary shard with the combine fused into the head's last kernel
+      (b200_fp8_lmhead_combined / b200_w4_lmhead_combined); the statistics returned are
+      global.
+
+    Every rank must make the same sequence of calls with the same row count M <= M_cap."""
 
     def __init__(self, M_cap: int, device: torch.device, group=None):
         import torch.distributed._symmetric_memory as symm_mem
@@ -120,22 +128,69 @@ class P2PCombiner:
         self.handle = symm_mem.rendezvous(self.buf, group)
         ptrs = [self.handle.get_remote_tensor(q, (nbytes,), torch.uint8).data_ptr() for q in range(self.world)]
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
-        self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+        self.counters = torch.zeros(M_cap, dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group)                 # every rank's buffer is zero before any rank stores
+
+    def _stats(self, M, dev, stats_out=None):
+        if stats_out is not None:
+            return stats_out
+        return (torch.empty(M, dtype=torch.float32, device=dev), torch.empty(M, dtype=torch.int64, device=dev),
+                torch.empty(M, dtype=torch.float32, device=dev))
 
     def __call__(self, mx: torch.Tensor, arg: torch.Tensor, lse: torch.Tensor):
         L = self._lib
         M = mx.numel()
         arg64 = arg if arg.dtype == torch.int64 else arg.to(torch.int64)
-        gm = torch.empty(M, dtype=torch.float32, device=mx.device)
-        ga = torch.empty(M, dtype=torch.int64, device=mx.device)
-        gl = torch.empty(M, dtype=torch.float32, device=mx.device)
+        gm, ga, gl = self._stats(M, mx.device)
         L.check(self.lib.b200_p2p_combine_row_stats(L.ptr(mx), L.ptr(arg64), L.ptr(lse), M, self.M_cap,
-                                                    L.ptr(self.peers), self.rank, self.world, L.ptr(self.counter),
-                                                    L.ptr(gm), L.ptr(ga), L.ptr(gl), L.stream_ptr()),
+                                                    L.ptr(self.peers), self.rank, self.world,
+                                                    L.ptr(self.counters), L.ptr(gm), L.ptr(ga), L.ptr(gl),
+                                                    L.stream_ptr()),
                 "b200_p2p_combine_row_stats")
         return gm, ga, gl
+
+    def fp8_head(self, x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset: int,
+                 want_logits: bool = True, out: torch.Tensor | None = None, stats_out: tuple | None = None):
+        """(logits of this shard | None, global max, global argmax, global logsumexp)."""
+        from . import fp8_target_lmhead as F8
+        from ._workspace import workspace
+        L = self._lib
+        F8._check(x, wq, ws)
+        M, K = x.shape
+        N = wq.shape[0]
+        y = (out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)) \
+            if want_logits else None
+        mx, arg, lse = self._stats(M, x.device, stats_out)
+        wsp = workspace(x.device)
+        L.check(self.lib.b200_fp8_lmhead_combined(
+            L.ptr(x), M, K, L.ptr(wq), L.ptr(ws), N, int(vocab_offset), L.ptr(y), N if y is None else y.stride(0),
+            L.ptr(mx), L.ptr(arg), L.ptr(lse), None, None, L.ptr(wsp), wsp.numel(),
+            L.ptr(self.peers), self.rank, self.world, L.ptr(self.counters), self.M_cap, L.stream_ptr()),
+            "b200_fp8_lmhead_combined")
+        L.debug_check("b200_fp8_lmhead_combined")
+        return y, mx, arg, lse
+
+    def w4_head(self, x: torch.Tensor, p, vocab_offset: int, want_logits: bool = True,
+                stats_out: tuple | None = None):
+        """The W4 draft head (PackedW4, either format) on this rank's shard: (logits of this
+        shard sliced to p.n | None, global max, global argmax, global logsumexp)."""
+        from ._workspace import workspace
+        L = self._lib
+        L.require_cuda("w4 head", x, p.wq, p.wsz)
+        M, K = x.shape
+        if K != p.k or x.dtype not in (torch.bfloat16, torch.float16) or not x.is_contiguous():
+            raise ValueError("w4 head: x must be a contiguous bf16/f16 [M, K] tensor matching the pack")
+        y = torch.empty(M, p.n_pad, dtype=torch.bfloat16, device=x.device) if want_logits else None
+        mx, arg, lse = self._stats(M, x.device, stats_out)
+        wsp = workspace(x.device)
+        L.check(self.lib.b200_w4_lmhead_combined(
+            1 if p.sym else 0, L.ptr(x), 0 if x.dtype == torch.bfloat16 else 1, M, K, L.ptr(p.wq), L.ptr(p.wsz),
+            p.n_pad, p.n, int(vocab_offset), L.ptr(y), p.n_pad, L.ptr(mx), L.ptr(arg), L.ptr(lse),
+            L.ptr(wsp), wsp.numel(), L.ptr(self.peers), self.rank, self.world, L.ptr(self.counters),
+            self.M_cap, L.stream_ptr()), "b200_w4_lmhead_combined")
+        L.debug_check("b200_w4_lmhead_combined")
+        return (y[:, :p.n] if y is not None else None), mx, arg, lse
 
 
 def shard_fp8_head(wq: torch.Tensor, ws: torch.Tensor, rank: int, world: int):

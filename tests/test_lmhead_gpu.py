@@ -306,3 +306,29 @@ def test_w4_graph_replay(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(yg, W4.gemm_w4a16(x, p))
+
+
+def test_fp8_tc_split_pairs_with_busy_sms(cuda):
+    """A tcgen05 head whose block pairs are split between CTAs, launched while a long W4 head
+    on another stream holds the SMs: its CTAs start in waves, not all at once. The split pairs
+    are finished by whichever CTA arrives last, which waits only for CTAs already running, so
+    the call completes, with the error word clear and every output identical, bit for bit, to
+    the same call made alone."""
+    N, K, M = 128 * 75, 2560, 64                   # 38 pairs x 20 K-blocks over the SMs: splits
+    wq, ws, _ = _fp8_weight(N, K, 21, cuda)
+    x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    ref = F8.fp8_lmhead(x, wq, ws)
+    torch.cuda.synchronize()
+    big = W4.pack_w4a16((torch.randn(151936, K, device=cuda) * 0.02).bfloat16())
+    xb = torch.randn(4, K, device=cuda, dtype=torch.bfloat16)
+    s_busy, s_head = torch.cuda.Stream(), torch.cuda.Stream()
+    for _ in range(3):
+        with torch.cuda.stream(s_busy):
+            for _ in range(4):
+                W4.gemm_w4a16_top(xb, big)
+        with torch.cuda.stream(s_head):
+            got = F8.fp8_lmhead(x, wq, ws)
+        torch.cuda.synchronize()
+        for a, b in zip(ref, got):
+            assert torch.equal(a, b)
+    assert P._lib.lmhead().b200_lmhead_error(1) == 0

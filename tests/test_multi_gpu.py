@@ -1,7 +1,9 @@
 """Two ranks on two GPUs (skipped with fewer): the vocabulary-sharded FP8 head combined over
-NVLink peer memory (P2PCombiner, one kernel per rank) matches the unsharded call (argmax
-exact; max and logsumexp within 1e-4, since the shards split the fp32 block sums between CTAs
-differently), repeatedly and inside a CUDA graph; the NCCL all-gather path agrees too. Ranks are spawned processes on
+NVLink peer memory (P2PCombiner: the standalone combine kernel, and the head with the combine
+fused into its last kernel, at the tcgen05 and the GEMV row counts) matches the unsharded
+call (argmax exact; max and logsumexp within 1e-4, since the shards split the fp32 block sums
+between CTAs differently), repeatedly and inside a CUDA graph; the NCCL all-gather path
+agrees too, and so does the sharded W4 draft head with its fused combine. Ranks are spawned processes on
 127.0.0.1 with a short process-group timeout, joined with a time limit."""
 from __future__ import annotations
 
@@ -36,14 +38,28 @@ def _rank(rank: int, port: int, q) -> None:
         comb = P.sharded.P2PCombiner(64, dev)
         errs = []
         for it in range(3):
-            x = torch.randn(M, K, device=dev, dtype=torch.bfloat16, generator=g)
+            x = torch.randn(M if it != 1 else 5, K, device=dev, dtype=torch.bfloat16, generator=g)
             _, mx, arg, lse = F8.fp8_lmhead(x, wq, ws, want_logits=False)
             _, m_, a_, l_ = F8.fp8_lmhead(x, wq[r0:r1], ws[r0 // 128:r1 // 128], vocab_offset=r0, want_logits=False)
             cm, ca, cl = comb(m_, a_, l_)
             nm, na, nl = P.sharded.combine_row_stats(m_, a_, l_)
+            # the head with the combine fused into its last kernel
+            _, fm, fa, fl = comb.fp8_head(x, wq[r0:r1], ws[r0 // 128:r1 // 128], r0, want_logits=False)
             torch.cuda.synchronize(dev)
             errs.append((bool(torch.equal(ca, arg)), float((cm - mx).abs().max()), float((cl - lse).abs().max()),
                          bool(torch.equal(na, ca)), float((nl - cl).abs().max())))
+            errs.append((bool(torch.equal(fa, arg)), float((fm - mx).abs().max()), float((fl - lse).abs().max()),
+                         bool(torch.equal(fa, ca)), float((fl - cl).abs().max())))
+        # the W4 draft head, sharded on 16-row strips, combined inside its last kernel
+        W4 = P.draft_w4_lmhead
+        wd = (torch.randn(1000, K, device=dev, generator=g) * 0.02).bfloat16()
+        xd = torch.randn(4, K, device=dev, generator=g).bfloat16()
+        s0, s1 = (0, 512) if rank == 0 else (512, 1000)
+        _, dm, da, dl = W4.gemm_w4a16_top(xd, W4.pack_w4a16(wd))
+        _, wm, wa, wl = comb.w4_head(xd, W4.pack_w4a16(wd[s0:s1]), s0, want_logits=False)
+        torch.cuda.synchronize(dev)
+        errs.append((bool(torch.equal(wa, da)), float((wm - dm).abs().max()), float((wl - dl).abs().max()),
+                     True, 0.0))
         # the same combine inside a CUDA graph, replayed twice
         x = torch.randn(M, K, device=dev, dtype=torch.bfloat16, generator=g)
         _, mx, arg, lse = F8.fp8_lmhead(x, wq, ws, want_logits=False)

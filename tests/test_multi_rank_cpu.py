@@ -144,3 +144,17 @@ def test_expert_id_sharding_matches_per_shard_oracle():
             own = ids[(ids >= r * e_loc) & (ids < (r + 1) * e_loc)] - r * e_loc
             LO.manage(ref[r], own, 16, 16)
             assert LO.state_digest(states[r]) == LO.state_digest(ref[r])
+
+
+def test_combine_poisoned_shard_gives_nan_and_minus_one():
+    """A shard whose statistics are poisoned (NaN max, as a head whose bounded wait ran out
+    reports them) makes the combined max / logsumexp NaN and the argmax -1, the rule the CUDA
+    combines follow; finite shards combine as usual (ties go to the first shard)."""
+    import importlib
+    import torch
+    P = importlib.import_module("r9700-lru-expert-cache_b200")
+    a = (torch.tensor([1.0, 2.0]), torch.tensor([3, 4]), torch.tensor([1.5, 2.5]))
+    b = (torch.tensor([float("nan"), 2.0]), torch.tensor([-1, 9]), torch.tensor([float("nan"), 2.1]))
+    mx, arg, lse = P.sharded.combine_row_stats_local([a, b])
+    assert torch.isnan(mx[0]) and torch.isnan(lse[0]) and int(arg[0]) == -1
+    assert float(mx[1]) == 2.0 and int(arg[1]) == 4 and torch.isfinite(lse[1])

@@ -5,7 +5,7 @@ and 12: the other ranks' rows are written into the buffer by the test before the
 tagged words those ranks' stores leave there, so one launch runs the whole combine and no
 kernel waits on another. Both match the NCCL path's combine (b200_combine_row_stats over the
 float64 triples) bit for bit, over successive calls that alternate the buffer parity and
-advance the tag. A rank whose rows never arrive, or whose rows carry a stale call's tag, makes the bounded
+advance the tag; every token keeps its own call counter. A rank whose rows never arrive, or whose rows carry a stale call's tag, makes the bounded
 wait give up after about a second with error word 2, and the context stays usable."""
 from __future__ import annotations
 
@@ -55,11 +55,11 @@ def _combine_ref(lib, ranks, dev):
     return out
 
 
-def _call(lib, rows, M, M_cap, peers, rank, world, counter, dev):
+def _call(lib, rows, M, M_cap, peers, rank, world, counters, dev):
     out = _outputs(M, dev)
     mx, arg, lse = rows
     rc = lib.b200_p2p_combine_row_stats(L.ptr(mx), L.ptr(arg), L.ptr(lse), M, M_cap, L.ptr(peers), rank, world,
-                                        L.ptr(counter), L.ptr(out[0]), L.ptr(out[1]), L.ptr(out[2]),
+                                        L.ptr(counters), L.ptr(out[0]), L.ptr(out[1]), L.ptr(out[2]),
                                         L.stream_ptr())
     assert rc == 0
     return out
@@ -76,7 +76,7 @@ def _buffer(lib, world, M_cap, dev):
     assert nbytes == 2 * world * M_cap * WORDS * 8
     buf = torch.zeros(nbytes // 8, device=dev, dtype=torch.int64)
     peers = torch.tensor([buf.data_ptr()] * world, device=dev, dtype=torch.int64)
-    return buf, buf.view(2, world, M_cap, WORDS), peers, torch.zeros(1, device=dev, dtype=torch.int64)
+    return buf, buf.view(2, world, M_cap, WORDS), peers, torch.zeros(M_cap, device=dev, dtype=torch.int64)
 
 
 @pytest.mark.parametrize("M,M_cap", [(64, 64), (40, 64), (200, 256)])
@@ -88,7 +88,7 @@ def test_single_rank_round_trip(cuda, M, M_cap):
         got = _call(lib, rows, M, M_cap, peers, 0, 1, counter, cuda)
         _same(got, _combine_ref(lib, [rows], cuda))
     torch.cuda.synchronize()
-    assert int(counter.item()) == 3
+    assert torch.all(counter[:M] == 3) and torch.all(counter[M:] == 0)     # per-token counters
     assert lib.b200_lmhead_error(1) == 0
 
 
@@ -133,7 +133,7 @@ def test_missing_or_stale_rows_time_out(cuda):
     got = _call(lib, rows, M, M_cap, peers, 0, world, counter, cuda)
     _same(got, _combine_ref(lib, [rows, rows], cuda))
     torch.cuda.synchronize()
-    assert lib.b200_lmhead_error(1) == 0 and int(counter.item()) == 3
+    assert lib.b200_lmhead_error(1) == 0 and torch.all(counter == 3)
 
 
 def test_empty_call_does_not_count(cuda):
@@ -148,11 +148,11 @@ def test_empty_call_does_not_count(cuda):
                                                 L.ptr(counter), None, None, None, L.stream_ptr())
             assert rc == 0
             continue
-        call = int(counter.item())
+        call = int(counter[0].item())
         ranks = [_stats(M, 300 + 10 * k + r, cuda) for r in range(world)]
         view[call & 1, 1, :M] = _tagged(*ranks[1], call + 1).to(cuda)
         got = _call(lib, ranks[rank], M, M_cap, peers, rank, world, counter, cuda)
         _same(got, _combine_ref(lib, ranks, cuda))
     torch.cuda.synchronize()
-    assert int(counter.item()) == 2
+    assert torch.all(counter == 2)
     assert lib.b200_lmhead_error(1) == 0
