@@ -91,6 +91,7 @@ struct Params {
   int x_off, xs_off, ring_off;
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
   int kw;            // tcgen05 path: 128-K blocks per stage
+  int cs_off;        // tcgen05 path: per-accumulator scale vectors in shared memory
   float* px;         // tcgen05 path: partial accumulators of blocks split along K
   int* flags;        // tcgen05 path: split pairs' tickets and ready flags
   // vocabulary-sharded combine fused into the statistics merge (peers == nullptr: none)
@@ -571,8 +572,9 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
 // is written.
 
 constexpr int TC_ISSUERS = 2;                       // MMA-issuing warps, one per block of a pair
+constexpr int TC_SCALE_WARP = 1 + TC_ISSUERS;     // writes the epilogue's per-unit scale vectors
 constexpr int TC_EPI_WARPS = 8;
-constexpr int TC_THREADS = 32 * (1 + TC_ISSUERS + TC_EPI_WARPS);
+constexpr int TC_THREADS = 32 * (2 + TC_ISSUERS + TC_EPI_WARPS);
 constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_MAX_BUF = 16;
 constexpr int TC_TILE_W = 128 * 128;
@@ -646,6 +648,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// (a0, a1) += (v0 * c0, v1 * c1): two fused multiply-adds, each rounded once (round to nearest),
+// in one packed instruction.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float v0, float v1, float c0, float c1) {
+  unsigned long long a = ((unsigned long long)__float_as_uint(a1) << 32) | __float_as_uint(a0);
+  const unsigned long long v = ((unsigned long long)__float_as_uint(v1) << 32) | __float_as_uint(v0);
+  const unsigned long long c = ((unsigned long long)__float_as_uint(c1) << 32) | __float_as_uint(c0);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(v), "l"(c));
+  a0 = __uint_as_float((uint32_t)a);
+  a1 = __uint_as_float((uint32_t)(a >> 32));
 }
 
 // The registers a tcgen05.ld writes are valid only after tcgen05.wait::ld; passing each value
@@ -870,6 +883,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   int* s_ticket = reinterpret_cast<int*>(tmem_slot + 2);       // [2 groups][2 parities]
   float* xs_s = reinterpret_cast<float*>(sm + p.xs_off);       // [KB][TPAD]
+  float* c_s = reinterpret_cast<float*>(sm + p.cs_off);        // [accumulator][TPAD]
   char* ring = sm + p.ring_off;
   b200::RowStat st[TPAD / TC_CHUNK];        // epilogue lanes l < 16: tokens 16 ch + l
 
@@ -879,7 +893,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       b200::mbar_init(&w_empty[i], TC_ISSUERS);
     }
     for (int i = 0; i < nbuf; ++i) {
-      b200::mbar_init(&a_full[i], 1);
+      b200::mbar_init(&a_full[i], 2);              // the MMAs' commit + the scale vector
       b200::mbar_init(&a_empty[i], 4);             // the four warps of the buffer's group
     }
     b200::mbar_init(xs_bar, 1);
@@ -951,6 +965,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   } else if (warp <= TC_ISSUERS) {
     // ---------------- MMA issuers: issuer `me` computes block 2p + me of every stage --------
+    // (one thread each, doing nothing else: its loop sets the pace of the whole pipeline)
     if (lane == 0) {
       const int me = warp - 1;
       const uint32_t idesc = (1u << 4)                        // D: f32
@@ -979,11 +994,56 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       b200::mbar_wait_bounded(done_bar, 0, deadline + WAIT_NS);
     }
     __syncwarp();
+  } else if (warp == TC_SCALE_WARP) {
+    // ---------------- scale vectors: for every accumulator, c[t] = ws[block, kb] * xs[kb][t],
+    // written into the accumulator's slot ahead of the MMAs (the slot is free once the epilogue
+    // has released the accumulator's previous use), so that the epilogue's per-unit work is one
+    // fused multiply-add per logit. The accumulator is complete (a_full) when its MMAs have
+    // landed AND its vector is written. Lane j holds the weight scales of units base + j, the
+    // next 32 units' already in flight.
+    const float* wsp = static_cast<const float*>(p.wscale);
+    auto load32 = [&](int base, float (&w)[2]) {
+      const int u = base + lane;
+      int pr, kb;
+      wk.unit(u, pr, kb);
+#pragma unroll
+      for (int me = 0; me < 2; ++me) {
+        const int blk = 2 * pr + me;
+        w[me] = (u < total && blk < nblk) ? __ldg(wsp + (long long)blk * KB + kb) : 0.f;
+      }
+    };
+    float wcur[2], wnext[2];
+    load32(0, wcur);
+    load32(32, wnext);
+    bool ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xs_bar, 0, deadline));
+    for (int it = 0; it < total && ok; ++it) {
+      if ((it & 31) == 0 && it > 0) {
+        wcur[0] = wnext[0];
+        wcur[1] = wnext[1];
+        load32(it + 32, wnext);
+      }
+      int pr, kb;
+      wk.unit(it, pr, kb);
+      const float* xk = xs_s + kb * TPAD;
+#pragma unroll
+      for (int me = 0; me < 2; ++me) {
+        const int kk = 2 * it + me, buf = kk % nbuf;
+        if (kk >= nbuf) ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_empty[buf], ((kk / nbuf) - 1) & 1, deadline));
+        if (!ok) break;
+        const float sw = __shfl_sync(0xffffffffu, wcur[me], it & 31);
+        float* c = c_s + buf * TPAD;
+#pragma unroll
+        for (int t = lane; t < TPAD; t += 32) c[t] = sw * xk[t];
+        __syncwarp();
+        if (lane == 0) b200::mbar_arrive(&a_full[buf]);
+      }
+    }
+    if (!ok && lane == 0) atomicExch(&g_lmhead_err, 1);
   } else {
     // ---------------- epilogue: group g handles block 2p + g of each pair ----------------
     // After a timed-out wait the warps carry on without touching TMEM (so every warp still
     // reaches the final barrier) and the error word reports the call.
-    const int ew = warp - 1 - TC_ISSUERS;     // 0..7
+    const int ew = warp - 2 - TC_ISSUERS;     // 0..7
     const int g = ew >> 2;
     const int qd = warp & 3;                  // TMEM lane quarter this warp may access
     const int row = 32 * qd + lane;           // row of the 128-row block held by this lane
@@ -1000,8 +1060,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       float acc[TPAD];
 #pragma unroll
       for (int j = 0; j < TPAD; ++j) acc[j] = 0.f;
-      const float* wsrow = static_cast<const float*>(p.wscale) + (long long)(real ? blk : 0) * KB;
-      const float wsv = (lane < KB && real) ? __ldg(wsrow + lane) : 0.f;
       int j1 = j0;
       for (;; ++it) {
         int p2, kb;
@@ -1010,12 +1068,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (p2 != pr) break;
         j1 = kb;
         const int kk = 2 * it + g, buf = kk % nbuf;
-        const float sw = (KB <= 32) ? __shfl_sync(0xffffffffu, wsv, kb & 31) : (real ? __ldg(wsrow + kb) : 0.f);
         if (ok) ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&a_full[buf], (kk / nbuf) & 1, deadline));
         if (!ok) continue;
         tc_fence_after();
         const uint32_t ta = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * TPAD);
-        const float4* xs4 = reinterpret_cast<const float4*>(xs_s + kb * TPAD);
+        const float4* c4 = reinterpret_cast<const float4*>(c_s + buf * TPAD);   // ws * xs per token
 #pragma unroll
         for (int h = 0; h < TPAD / 32; ++h) {
           float v[32];
@@ -1024,11 +1081,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tmem_values_after_wait(v);
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const float4 xv = xs4[(32 * h + j) >> 2];
-            acc[32 * h + j] = fmaf(v[j], sw * xv.x, acc[32 * h + j]);
-            acc[32 * h + j + 1] = fmaf(v[j + 1], sw * xv.y, acc[32 * h + j + 1]);
-            acc[32 * h + j + 2] = fmaf(v[j + 2], sw * xv.z, acc[32 * h + j + 2]);
-            acc[32 * h + j + 3] = fmaf(v[j + 3], sw * xv.w, acc[32 * h + j + 3]);
+            const float4 cv = c4[(32 * h + j) >> 2];
+            ffma2(acc[32 * h + j], acc[32 * h + j + 1], v[j], v[j + 1], cv.x, cv.y);
+            ffma2(acc[32 * h + j + 2], acc[32 * h + j + 3], v[j + 2], v[j + 3], cv.z, cv.w);
           }
         }
         tc_fence_before();
@@ -1155,8 +1210,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (STATS) {
     // the ring is idle now: the per-warp row statistics go there
     b200::RowStat* red = reinterpret_cast<b200::RowStat*>(ring);
-    if (warp > TC_ISSUERS) {
-      const int ew = warp - 1 - TC_ISSUERS;
+    if (warp > TC_SCALE_WARP) {
+      const int ew = warp - 2 - TC_ISSUERS;
       for (int i = 0; i < 64; i += 32) red[ew * 64 + i + lane] = b200::RowStat{-INFINITY, 0x7fffffff, 0.f};
       __syncwarp();
       if (lane < TC_CHUNK) {
@@ -1584,8 +1639,10 @@ static_assert(3LL * TC_MAX_GRID * 64 * 12 <= PART_CAP, "statistics slots: CTAs +
 // smem bytes or -1.
 int plan_tc(Params& p, int tpad) {
   const int KB = p.K / 128;
+  const int nbuf = min(TC_MAX_BUF, 512 / tpad);             // TMEM accumulators
   p.xs_off = TC_HDR;
-  p.x_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;          // 8 warps x [16][33] fp32 tiles
+  p.cs_off = (p.xs_off + tpad * KB * 4 + 15) & ~15;         // nbuf x [tpad] fp32 scale vectors
+  p.x_off = (p.cs_off + nbuf * tpad * 4 + 15) & ~15;        // 8 warps x [16][33] fp32 tiles
   p.ring_off = (p.x_off + TC_EPI_WARPS * TC_CHUNK * 33 * 4 + 1023) & ~1023;
   const int avail = SMEM_CAP - 1024 - p.ring_off;
   const int stage = TC_PAIR_W + tpad * 128;
@@ -1593,7 +1650,7 @@ int plan_tc(Params& p, int tpad) {
   if (nstage < 2) return -1;
   p.kw = 1;
   p.nstage = nstage;
-  p.kps = min(TC_MAX_BUF, 512 / tpad);     // TMEM accumulators
+  p.kps = nbuf;
   return 1024 + p.ring_off + nstage * stage;
 }
 
