@@ -332,3 +332,27 @@ def test_fp8_tc_split_pairs_with_busy_sms(cuda):
         for a, b in zip(ref, got):
             assert torch.equal(a, b)
     assert P._lib.lmhead().b200_lmhead_error(1) == 0
+
+
+@pytest.mark.parametrize("nblk", [296, 297, 298, 301, 447, 1187, 8, 3])
+def test_fp8_tc_work_splits(cuda, nblk):
+    """Vocabulary sizes around the tcgen05 work split on 148 SMs (whole pairs per CTA, the rest
+    split by 128-K units): a pair count that is a multiple of the CTA count (296 blocks = 148
+    pairs), one pair more (298 blocks), odd block counts (297, 301), several extra pairs (447,
+    1187: the full head) and fewer pairs than CTAs (8, 3 blocks). Logits within the reference bound,
+    statistics against the oracle, repeated calls identical."""
+    N, K, M = 128 * nblk, 2560, 64
+    wq, ws, wdq = _fp8_weight(N, K, nblk, cuda)
+    g = torch.Generator(device=cuda).manual_seed(10_000 + nblk)       # not the weight's stream
+    x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16, generator=g)
+    y, mx, arg, lse = F8.fp8_lmhead(x, wq, ws)
+    rq, rs = Q.group_quant_fp8(x, 128)
+    ref = Q.fp8_block_gemm_ref(rq, rs, wdq)
+    rel = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < REL_FP8, rel
+    _check_stats(f"nblk={nblk}", ref, mx, arg, lse)
+    again = F8.fp8_lmhead(x, wq, ws)
+    for a, b in zip((y, mx, arg, lse), again):
+        assert torch.equal(a, b)
+    assert P._lib.lmhead().b200_lmhead_error(1) == 0
+    del wdq, ref
