@@ -531,6 +531,86 @@ def sharded_parity(P, x, shards, rank: int, world: int, dev, combined) -> dict:
                      "same x, rebuilt on every rank; argmax exact, max/lse < 1e-4"}
 
 
+def w4_sharded_bench(P, x4, shards, rank: int, world: int, dev, combiner) -> dict:
+    """The W4 draft head (the reference's asymmetric int4 format, M=4 rows x K=2560) on this
+    rank's vocabulary shard, with the (max, argmax, logsumexp) combine fused into its last kernel
+    at N > 1 (the sharded MTP.get_top_tokens): us per step in CUDA graphs over a weight pool
+    larger than L2, max over ranks; aggregate GB/s = the whole head's algorithmic bytes / that
+    time. At N > 1 the combined result is checked against the unsharded head (rebuilt on every
+    rank from the per-rank weight seeds 200 + r): argmax exact."""
+    W4 = P.draft_w4_lmhead
+    r0, r1 = shards[rank]
+
+    def shard_weight(r):
+        a, b = shards[r]
+        g = torch.Generator(device=dev).manual_seed(200 + r)
+        return (torch.randn(b - a, K_HID, device=dev, generator=g) * 0.02).bfloat16()
+    pk = W4.pack_w4a16(shard_weight(rank))
+    copies = max(1, math.ceil(POOL_BYTES / pk.nbytes))
+    pool = [pk] + [W4.PackedW4(pk.wq.clone(), pk.wsz.clone(), pk.n, pk.n_pad, pk.k) for _ in range(copies - 1)]
+    mx = torch.empty(4, dtype=torch.float32, device=dev)
+    arg = torch.empty(4, dtype=torch.int64, device=dev)
+    lse = torch.empty(4, dtype=torch.float32, device=dev)
+
+    def step(i):
+        q = pool[i % len(pool)]
+        if combiner is not None:
+            return combiner.w4_head(x4, q, r0, want_logits=False, stats_out=(mx, arg, lse))[1:]
+        return W4.gemm_w4a16_top(x4, q, vocab_offset=r0, want_logits=False)[1:]
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(len(pool)):
+            step(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    reps = 8 * len(pool)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for i in range(reps):
+            step(i)
+    gr.replay()
+    torch.cuda.synchronize(dev)
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    times = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        gr.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        times.append(a.elapsed_time(b) * 1e3 / reps)
+    gr.reset()
+    del gr
+    us = statistics.median(times)
+    t = torch.tensor([us], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t[0])
+    res = {"us_per_step": us, "M": 4, "rows_per_gpu": r1 - r0,
+           "GB_s": w4_bytes(N_VOCAB, K_HID, 4) / us / 1e3,
+           "combine": None if world == 1 else "nvlink peer memory, fused into the head's statistics merge"}
+    if world > 1:
+        got = [v.clone() for v in step(0)]
+        full = W4.pack_w4a16(torch.cat([shard_weight(r) for r in range(world)]))
+        _, fmx, farg, flse = W4.gemm_w4a16_top(x4, full, want_logits=False)
+        torch.cuda.synchronize(dev)
+        n_arg = int((got[1] != farg).sum())
+        dl = float((got[2] - flse).abs().max())
+        bad = torch.tensor([float(n_arg), dl], dtype=torch.float64, device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        res["parity"] = {"parity_ok": bool(bad[0] == 0 and bad[1] < 1e-4), "argmax_mismatches": int(bad[0]),
+                         "max_abs_dlse": float(bad[1])}
+        del full
+    del pool
+    return res
+
+
 def probe_ceiling(P, dev, nbytes: int) -> float:
     """Read-only control over the same bytes (hcq_stream_probe) -> GB/s."""
     buf = torch.empty(POOL_BYTES // nbytes * nbytes + nbytes, dtype=torch.uint8, device=dev)
@@ -863,9 +943,13 @@ def main():
         combined = [t.clone() for t in step(0)]
         parity = sharded_parity(P, x, shards, rank, world, dev, combined)
 
-    # ---- secondary: expert-sharded LRU on every rank, then rank-0 extras ------------------
-    lru = None
+    # ---- secondary: expert-sharded LRU and vocab-sharded W4 draft head on every rank, then
+    # rank-0 extras ----------------------------------------------------------------------------
+    lru = w4s = None
     if not args.no_extras:
+        torch.manual_seed(4)
+        w4s = w4_sharded_bench(P, torch.randn(4, K_HID, device=dev, dtype=torch.bfloat16), shards, rank,
+                               world, dev, combiner)
         lru = lru_bench(P, rank, world, dev)
         tl = torch.tensor([lru["us_per_layer"]], dtype=torch.float64, device=dev)
         if world > 1:
@@ -932,6 +1016,7 @@ def main():
                 "nvlink peer memory, fused into the head's statistics merge" if combiner else "nccl all_gather"),
             "clocks": clk.summary(),
             "lru": lru,
+            "w4_draft_head_sharded": w4s,
             "ops": ops,
             "ops_cpu_baseline": cpu_ops,
         }
