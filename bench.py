@@ -257,10 +257,17 @@ def time_graph(fn, reps: int, dev) -> float:
     return statistics.median(out)
 
 
+def zipf_routes(rng, E: int, rows: int, topk: int = TOPK, s: float = 1.1) -> np.ndarray:
+    """Synthetic router output: per token, top_k distinct experts drawn with Zipf(s)
+    popularity (expert e has weight (e + 1)^-s), int32 [rows, topk]."""
+    p = np.arange(1, E + 1, dtype=float) ** -s
+    p /= p.sum()
+    return np.stack([rng.choice(E, size=topk, replace=False, p=p) for _ in range(rows)]).astype(np.int32)
+
+
 def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
     """52 layers of the fused LRU update on this rank's expert shard, captured once per layer
     set and replayed with fresh Zipf(1.1) routing (T=5 rows x top-10) each replay."""
-    from oracle import lru_oracle as LO      # routing generator only (seeded Zipf, host side)
     e_loc = E_EXPERTS // world
     s_loc = max(1, (S_SLOTS * e_loc + E_EXPERTS - 1) // E_EXPERTS)
     rng = np.random.default_rng(1234)
@@ -271,7 +278,7 @@ def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
                                           step=s_loc, max_inserts=64))
     mk = 5 * TOPK
     R = reps + 3
-    routes = np.stack([np.stack([LO.zipf_rows(rng, E_EXPERTS, 5, TOPK).ravel() for _ in range(LAYERS)])
+    routes = np.stack([np.stack([zipf_routes(rng, E_EXPERTS, 5).ravel() for _ in range(LAYERS)])
                        for _ in range(R)]).astype(np.int32)            # [R, 52, mk]
     routes_d = P.sharded.local_expert_ids(torch.as_tensor(routes, device=dev), rank, e_loc)
     ids = torch.zeros(LAYERS, mk, dtype=torch.int32, device=dev)
@@ -482,6 +489,86 @@ def ops_bench(P, dev) -> dict:
     us = time_graph(ms_big, 2 * len(ins), dev)
     nb = Tm * TOPK * K_HID * 2 + Tm * K_HID * 2
     res[f"moe_sum_T{Tm}_k10"] = {"us_per_call": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk}
+    del ins, osum
+    res.update(moe_gemm_bench(P, dev))
+    return res
+
+
+MOE_INTER = 320          # the experts' intermediate width: gate_up N = 2 x 320, down K = 320
+
+
+def moe_weights(n_e: int, N: int, K: int, g) -> tuple:
+    """Random B200-packed MXFP4 expert weights (the kernel's timing does not depend on values)."""
+    NS, G = N // 16, K // 32
+    wq = torch.randint(0, 256, (n_e, NS, G, 256), generator=g, dtype=torch.uint8, device=g.device)
+    ws = torch.randint(118, 128, (n_e, NS, G, 16), generator=g, dtype=torch.uint8, device=g.device)
+    return wq, ws, torch.full((n_e, N), 127, dtype=torch.uint8, device=g.device)
+
+
+def moe_expert_bytes(N: int, K: int) -> int:
+    return (N // 16) * (K // 32) * 272 + N
+
+
+def moe_cases(P, dev, T: int, routings: int, rng, lay) -> list:
+    """`routings` Zipf routings of T tokens through the cache: (hot align, cold align,
+    distinct resident slots touched, distinct other experts touched) each."""
+    cases = []
+    for _ in range(routings):
+        ids = torch.as_tensor(zipf_routes(rng, lay.E, T).ravel(), device=dev)
+        hot, cold = lay.fused(ids)
+        hot, cold = tuple(t.clone() for t in hot), tuple(t.clone() for t in cold)
+        nh = len(set(hot[1][:int(hot[2].item()) // 16].tolist()))
+        nc = len(set(cold[1][:int(cold[2].item()) // 16].tolist()))
+        cases.append((hot, cold, nh, nc))
+    return cases
+
+
+def moe_gemm_bench(P, dev, tokens=(1, 4, 20), routings: int = 8) -> dict:
+    """The grouped MXFP4 x FP8 MoE GEMM at decode: E=512 experts, 257 resident slots, top-10
+    Zipf(1.1) routing through r4d_lru_fused (the cache settled by 64 steps first). Per projection
+    the layer's two calls: the hot call over the resident copies (by slot), then the cold call
+    over the full tensors (by expert). gate_up N=640 K=2560 (token rows read top_k times);
+    down N=2560 K=320 with routed weights. `routings` routings rotate inside one CUDA graph; the
+    weights (0.9 GB) exceed L2. Bytes = the touched experts' packed strips and row exponents +
+    the activation rows + the bf16 outputs."""
+    MO = P.moe_ops
+    pk = peaks()["hbm_gbs"]
+    g = torch.Generator(device=dev).manual_seed(77)
+    E, S = E_EXPERTS, S_SLOTS
+    gu_full, gu_hot = moe_weights(E, 2 * MOE_INTER, K_HID, g), moe_weights(S, 2 * MOE_INTER, K_HID, g)
+    dn_full, dn_hot = moe_weights(E, K_HID, MOE_INTER, g), moe_weights(S, K_HID, MOE_INTER, g)
+    rng = np.random.default_rng(99)
+    lay = P.lru.LruLayer.warm(sorted(rng.choice(E, S, replace=False).tolist()), E, dev, step=S, max_inserts=64)
+    for _ in range(64):
+        lay.fused(torch.as_tensor(zipf_routes(rng, E, 20).ravel(), device=dev))
+    res = {}
+    for T in tokens:
+        mtk = T * TOPK
+        cases = moe_cases(P, dev, T, routings, rng, lay)
+        qx = (torch.randn(T, K_HID, device=dev) * 40).to(torch.float8_e4m3fn)
+        xs = torch.rand(T, device=dev) * 1e-2 + 1e-3
+        qd = (torch.randn(mtk, MOE_INTER, device=dev) * 40).to(torch.float8_e4m3fn)
+        xsd = torch.rand(mtk, device=dev) * 1e-2 + 1e-3
+        tw = torch.rand(mtk, device=dev)
+        y1 = torch.empty(mtk, 2 * MOE_INTER, dtype=torch.bfloat16, device=dev)
+        y2 = torch.empty(mtk, K_HID, dtype=torch.bfloat16, device=dev)
+        touched = statistics.mean(c[2] + c[3] for c in cases)
+        hot_share = statistics.mean(c[2] / max(1, c[2] + c[3]) for c in cases)
+        for name, N, K, full, hotw, x, xsc, topk, w, y in (
+                ("gate_up", 2 * MOE_INTER, K_HID, gu_full, gu_hot, qx, xs, TOPK, None, y1),
+                ("down", K_HID, MOE_INTER, dn_full, dn_hot, qd, xsd, 1, tw, y2)):
+            it = {"i": 0}
+
+            def call():
+                h, c, _, _ = cases[it["i"] % routings]
+                it["i"] += 1
+                MO.gemm_split(y, x, xsc, full, hotw, h, c, w, mtk, topk)
+            us = time_graph(call, 4 * routings, dev)
+            nb = touched * moe_expert_bytes(N, K) + x.numel() + 4 * x.shape[0] + mtk * N * 2
+            res[f"moe_{name}_T{T}"] = {"us_per_layer": us, "GB_s": nb / us / 1e3, "frac_hbm": nb / us / 1e3 / pk,
+                                       "experts_touched": touched, "resident_share": hot_share,
+                                       "calls": 2}
+    assert P._lib.lmhead().b200_moe_gemm_error(0) == 0
     return res
 
 
@@ -633,7 +720,7 @@ def probe_ceiling(P, dev, nbytes: int) -> float:
 # ---------------------------------------------------------------------------------------
 
 def run_op(args):
-    """One op alone, eager launches (what ncu captures): --op fp8|w4|lru|silu|gate|moe_sum|hquant."""
+    """One op alone, eager launches (what ncu captures): --op fp8|w4|lru|silu|gate|moe_sum|hquant|moe."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     P = load_pkg()
@@ -671,13 +758,25 @@ def run_op(args):
         x = torch.randn(args.m, K_HID, device=dev, dtype=torch.bfloat16)
         fn = lambda: P.fp8_hidden_quant.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
         nbytes = args.m * K_HID * 3 + args.m * 4
+    elif args.op == "moe":                       # --m tokens through one gate_up projection
+        g = torch.Generator(device=dev).manual_seed(77)
+        full = moe_weights(E_EXPERTS, 2 * MOE_INTER, K_HID, g)
+        hotw = moe_weights(S_SLOTS, 2 * MOE_INTER, K_HID, g)
+        rng = np.random.default_rng(99)
+        lay = P.lru.LruLayer.warm(sorted(rng.choice(E_EXPERTS, S_SLOTS, replace=False).tolist()), E_EXPERTS,
+                                  dev, step=S_SLOTS, max_inserts=64)
+        h, c, nh, nc = moe_cases(P, dev, args.m, 1, rng, lay)[0]
+        qx = (torch.randn(args.m, K_HID, device=dev) * 40).to(torch.float8_e4m3fn)
+        xs = torch.rand(args.m, device=dev) * 1e-2 + 1e-3
+        y = torch.empty(args.m * TOPK, 2 * MOE_INTER, dtype=torch.bfloat16, device=dev)
+        fn = lambda: P.moe_ops.gemm_split(y, qx, xs, full, hotw, h, c, None, args.m * TOPK, TOPK)
+        nbytes = (nh + nc) * moe_expert_bytes(2 * MOE_INTER, K_HID) + args.m * K_HID + y.numel() * 2
     elif args.op == "lru":
-        from oracle import lru_oracle as LO
         rng = np.random.default_rng(0)
         hot = sorted(rng.choice(E_EXPERTS, S_SLOTS, replace=False).tolist())
         lay = P.lru.LruLayer.warm(hot, E_EXPERTS, dev, stamps=torch.as_tensor(rng.permutation(S_SLOTS) + 1),
                                   step=S_SLOTS, max_inserts=64)
-        ids = torch.as_tensor(LO.zipf_rows(rng, E_EXPERTS, 5, TOPK).ravel().astype(np.int32), device=dev)
+        ids = torch.as_tensor(zipf_routes(rng, E_EXPERTS, 5).ravel(), device=dev)
         out = lay.new_align_outputs(ids.numel())
         fn = lambda: lay.fused(ids, out)
         nbytes = 0
@@ -704,7 +803,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the secondary measurements")
-    ap.add_argument("--op", choices=["fp8", "w4", "lru", "silu", "gate", "moe_sum", "hquant"], default=None,
+    ap.add_argument("--op", choices=["fp8", "w4", "lru", "silu", "gate", "moe_sum", "hquant", "moe"],
+                    default=None,
                     help="time one op alone with eager launches (for profiling)")
     ap.add_argument("--m", type=int, default=M_ROWS)
     ap.add_argument("--rows", type=int, default=N_VOCAB)

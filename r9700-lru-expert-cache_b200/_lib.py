@@ -60,6 +60,12 @@ LMHEAD_PROTOS = {
     "r4d_gemm_w4a16_nt_m64_last_error": (c_int, []),
     "r4d_gemm_w4a16_nt_m64_max_m": (c_int, []),
     "r4d_gemm_w4a16_nt_m64_group": (c_int, []),
+    "r4d_gemm_moe_mxfp4a8_nt_b16": (None, [c_long] * 10 + [c_int] * 8 + [c_long]),
+    "r4d_gemm_moe_mxfp4a8_nt_b16_last_error": (c_int, []),
+    "r4d_gemm_moe_mxfp4a8_nt_b16_block": (c_int, []),
+    "r4d_gemm_moe_mxfp4a8_nt_b16_group": (c_int, []),
+    "b200_moe_gemm_smem_bytes": (c_int, [c_int]),
+    "b200_moe_gemm_error": (c_int, [c_int]),
 }
 
 LIB_FILES = {"librlu.so": RLU_PROTOS, "libb200lmhead.so": LMHEAD_PROTOS}

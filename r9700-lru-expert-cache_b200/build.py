@@ -1,9 +1,10 @@
 """Build the two C-ABI shared libraries of this package, in-tree, for sm_100a.
 
 * ``librlu.so``       -- csrc/lru.cu: r4d_lru_manage / r4d_lru_fused / r4d_lru_gather.
-* ``libb200lmhead.so`` -- csrc/quant.cu + csrc/lmhead.cu + csrc/gate.cu + csrc/moe_sum.cu:
-  SiLU-mul FP8 quant, per-token (group) FP8 quant, FP8 and W4 lm_head GEMVs, the stream
-  control, the shared-expert gate and the routed experts' sum.
+* ``libb200lmhead.so`` -- csrc/quant.cu + csrc/lmhead.cu + csrc/gate.cu + csrc/moe_sum.cu +
+  csrc/moe_gemm.cu: SiLU-mul FP8 quant, per-token (group) FP8 quant, FP8 and W4 lm_head
+  GEMVs, the stream control, the shared-expert gate, the routed experts' sum and the grouped
+  MXFP4 x FP8 MoE GEMM.
 
 No fast math: the SiLU-quant parity needs IEEE division and the accurate expf.
 Usage: ``python build.py [--force]`` (also called by ``__graft_entry__.build()``).
@@ -23,7 +24,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
 
 LIBS = {
     "librlu.so": ["lru.cu"],
-    "libb200lmhead.so": ["quant.cu", "lmhead.cu", "gate.cu", "moe_sum.cu"],
+    "libb200lmhead.so": ["quant.cu", "lmhead.cu", "gate.cu", "moe_sum.cu", "moe_gemm.cu"],
 }
 
 

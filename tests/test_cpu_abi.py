@@ -29,7 +29,8 @@ def _declared(header: str) -> list[str]:
 
 
 @pytest.mark.parametrize("headers,lib", [(["r4d_lru.h"], "librlu.so"),
-                                         (["b200_lmhead.h", "b200_moe_tail.h"], "libb200lmhead.so")])
+                                         (["b200_lmhead.h", "b200_moe_tail.h", "b200_moe_gemm.h"],
+                                          "libb200lmhead.so")])
 def test_every_declared_symbol_is_exported(headers, lib):
     names = [n for h in headers for n in _declared(h)]
     assert len(names) >= 3
