@@ -500,13 +500,14 @@ MOE_INTER = 320          # the experts' intermediate width: gate_up N = 2 x 320,
 def moe_weights(n_e: int, N: int, K: int, g) -> tuple:
     """Random B200-packed MXFP4 expert weights (the kernel's timing does not depend on values)."""
     NS, G = N // 16, K // 32
-    wq = torch.randint(0, 256, (n_e, NS, G, 256), generator=g, dtype=torch.uint8, device=g.device)
-    ws = torch.randint(118, 128, (n_e, NS, G, 16), generator=g, dtype=torch.uint8, device=g.device)
+    wq = torch.randint(0, 256, (n_e, NS, G * 272), generator=g, dtype=torch.uint8, device=g.device)
+    ws = torch.randint(118, 128, (n_e, NS, 16, G), generator=g, dtype=torch.uint8, device=g.device)
+    wq[:, :, G * 256:] = ws.reshape(n_e, NS, 16 * G)
     return wq, ws, torch.full((n_e, N), 127, dtype=torch.uint8, device=g.device)
 
 
 def moe_expert_bytes(N: int, K: int) -> int:
-    return (N // 16) * (K // 32) * 272 + N
+    return (N // 16) * (K // 32) * 272
 
 
 def moe_cases(P, dev, T: int, routings: int, rng, lay) -> list:
@@ -529,8 +530,8 @@ def moe_gemm_bench(P, dev, tokens=(1, 4, 20), routings: int = 8) -> dict:
     the layer's two calls: the hot call over the resident copies (by slot), then the cold call
     over the full tensors (by expert). gate_up N=640 K=2560 (token rows read top_k times);
     down N=2560 K=320 with routed weights. `routings` routings rotate inside one CUDA graph; the
-    weights (0.9 GB) exceed L2. Bytes = the touched experts' packed strips and row exponents +
-    the activation rows + the bf16 outputs."""
+    weights (0.9 GB) exceed L2. Bytes = the touched experts' strip records (codes + exponents)
+    + the activation rows + the bf16 outputs."""
     MO = P.moe_ops
     pk = peaks()["hbm_gbs"]
     g = torch.Generator(device=dev).manual_seed(77)

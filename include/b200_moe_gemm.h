@@ -6,9 +6,12 @@
  * (patches/model_executor/layers/fused_moe/experts/r4d_mxfp4_moe.py.lru.diff L584-606).
  *
  * Packed layouts (B200 formats; codes and scales are the checkpoint's):
- *   wq   uint8 [E][N/16][K/32][32 lanes][8 B]  the codes in mma.sync A-fragment order
- *   ws   uint8 [E][N/16][K/32][16]            E8M0 exponents of each 16-row strip
- *   wref uint8 [E][N]                         per-row maximum exponent
+ *   wq   uint8 [E][N/16][K/32][32 lanes][8 B]  the codes in mma.sync A-fragment order (byte
+ *        4 h + r of lane 4 g + t: row g + 8 (r & 1), k = 16 h + 2 t + 8 (r >> 1) low nibble,
+ *        k + 1 high nibble)
+ *   ws   uint8 [E][N/16][16][K/32]            E8M0 exponents (the checkpoint's [E, N, K/32])
+ *   wref uint8 [E][N]                         per-row maximum exponent (the reference's
+ *                                             argument; accepted, not read)
  */
 #ifndef B200_MOE_GEMM_H
 #define B200_MOE_GEMM_H

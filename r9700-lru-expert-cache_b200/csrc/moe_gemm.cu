@@ -11,33 +11,38 @@
 //   tw is the routed weight of the row (absent: 1). Rows not named are left untouched.
 //
 // Decode shapes are small (a few routed rows per expert, 1 to 16 per block), so the weight
-// stream is the whole cost: each (block, 16-row strip of the expert's N outputs) is one unit
-// of work, and a CTA (one per SM) takes a contiguous run of the units of the live blocks,
-// whose count it reads on the device (so the launch is the same for every call and graph
-// capturable). Per CTA:
-//   * warp 0 lane 0 streams each unit's strip -- its nibbles for every 32-K group in one run,
-//     then its E8M0 scales -- with two 1-D bulk copies into a ring of shared-memory stages,
-//     and each block's activation rows (one bulk copy per live row) into the activation buffer
-//     once the consumers are done with the previous block's;
-//   * 4 consumer warps take the units in turn (unit q of the CTA to warp q % 4; the ring has a
-//     multiple of 4 stages, so a slot's previous use always belongs to the same warp, which
+// stream is the whole cost. A 16-row strip of an expert's N outputs is one record (its codes
+// for every 32-K group, then its E8M0 exponents); a unit of work is a block and a run of R
+// consecutive strips of its expert (R a power of two, records of R strips <= 24 KB: 1 strip at
+// K = 2560, 8 at K = 320), so that each unit is ONE bulk copy of 16-24 KB -- a bulk copy costs
+// the copy engine about a quarter microsecond however small, so several KB-sized copies per
+// unit would cap the stream. A CTA (one per SM) takes a contiguous run of the units of the
+// live blocks, whose count it reads on the device (so the launch is the same for every call
+// and graph capturable). Per CTA:
+//   * warp 0 lane 0 streams each unit's records into a ring of shared-memory stages, and each
+//     block's activation rows (one bulk copy per live row) into the activation buffer once the
+//     consumers are done with the previous block's -- meanwhile the new block's weights keep
+//     streaming, so a block boundary does not drain the ring;
+//   * 8 consumer warps take the units in turn (unit q of the CTA to warp q % 8; the ring has a
+//     multiple of 8 stages, so a slot's previous use always belongs to the same warp, which
 //     finished it before waiting on the slot again: the barrier's phase parity is never
-//     ambiguous). The strip is the A operand of mma.sync
-//     m16n8k16 f16: a lane's 8 bytes per group are its A fragments for two MMAs, and each
-//     e2m1 code becomes an f16 exactly (code bits shifted into place give e2m1 * 2^-14; one
-//     multiply by 2^(14 - (wref - s)) folds the group's scale, exactly while the result is
-//     representable in f16). The activation bytes become f16 exactly (cvt e4m3x2). fp32
-//     accumulation; the epilogue multiplies by 2^(wref - 127) (exact), the token's scale and
-//     the routed weight, and stores bf16.
+//     ambiguous). The strip is the A operand of mma.sync m16n8k16 f16: each byte of a lane's 8
+//     per group is one A register's two codes, which cvt.rn.f16x2.e2m1x2 turns into the two
+//     e2m1 values exactly; the activation bytes become f16 exactly too (cvt e4m3x2). Each group's
+//     two MMAs start from zero (32 products, fp32), and the group's sum is scaled by its
+//     exponent 2^(s - 127) in fp32 (exact) into the row's total -- no f16 range limit on the
+//     exponents. The epilogue multiplies by the token's scale and the routed weight and stores
+//     bf16.
 //   * rows beyond the block's live ones skip their MMA tile when all of 8..15 are padding.
 // Every wait is bounded (2 s) and reports a timeout through the error word instead of hanging.
 //
 // Packed layouts (B200 formats; codes and scales are the checkpoint's):
-//   wq   uint8 [E][N/16 strips][K/32 groups][32 lanes][8 bytes]; lane (g, t) of a group holds
-//        two 32-bit words, word h for k in [16 h, 16 h + 16): its nibble pair p (bits 4p and
-//        16 + 4p) is row (g + 8 (p & 1)), k = 16 h + 2 t + 8 (p >> 1) and that k + 1.
-//   ws   uint8 [E][N/16][K/32][16 rows] E8M0 exponents (the reference's ws_t, regrouped).
-//   wref uint8 [E][N] per-row reference exponent, the maximum of the row's scales.
+//   wq   uint8 [E][N/16 strips][272 K/32]: per strip the codes [K/32 groups][32 lanes][8 bytes],
+//        byte 4 h + r of lane (g, t) holding A register r of k-half h: row g + 8 (r & 1),
+//        k = 16 h + 2 t + 8 (r >> 1) in its low nibble and k + 1 in its high nibble; then the
+//        E8M0 exponents [16 rows][K/32].
+//   ws, wref: the checkpoint's exponents [E, N, K/32] and their per-row maximum [E, N], part
+//        of the reference's argument list; this kernel reads both from wq's records.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -50,11 +55,13 @@ namespace {
 
 constexpr int MOE_BLOCK = 16;             // rows per aligned block (moe_align block size)
 constexpr int MOE_GROUP = 32;             // K per E8M0 exponent
-constexpr int MOE_NC = 4;                 // consumer warps
+constexpr int MOE_NC = 16;                // consumer warps
+constexpr int MOE_PAIRS = MOE_NC / 2;     // ... in pairs: one unit per pair, K split between them
 constexpr int MOE_THREADS = 32 * (1 + MOE_NC);
-constexpr int MOE_MAX_STAGES = 16;
+constexpr int MOE_MAX_STAGES = 32;
 constexpr int MOE_SMEM_CAP = 227 * 1024;
-constexpr int MOE_HDR = 512;              // barriers and the two buffers' row ids
+constexpr int MOE_HDR = 640;              // barriers (66 x 8 B) and the block's row ids (64 B)
+constexpr int MOE_XCH = 2 * 32 * 8 * 4;   // per pair: two buffers of 8 partial sums per lane
 constexpr uint64_t MOE_WAIT_NS = 2000000000ull;
 
 __device__ int g_moe_err = 0;             // 1 = a pipeline wait timed out
@@ -63,28 +70,45 @@ struct MoeParams {
   const uint8_t* qx;       // e4m3 [tokens, K]; row i of the GEMM reads token i / top_k
   const float* xs;         // fp32 [tokens]
   const uint8_t* wq;
-  const uint8_t* ws;
-  const uint8_t* wref;
   __nv_bfloat16* y;        // [mtk, N]
   const int* sorted;       // [em]
   const int* eids;         // [em / 16]
   const int* npad;         // [1]
   const float* tw;         // [mtk] or nullptr
   int em, mtk, top_k, K, N;
-  int nstage, stage_bytes, xrow, x_off, ring_off;
+  int nstage, stage_bytes, xrow, x_off, ring_off, run;   // run = R strips per unit
+  int xch_off;                                            // the pairs' exchange buffers
 };
 
-// e2m1 nibble pairs at bits (0..3, 16..19) of w -> f16x2 of e2m1 * 2^-14, exactly: the three
-// magnitude bits land in f16 bits 9..11 (the f16 with that exponent/mantissa pattern is the
-// e2m1 value scaled by 2^-14, subnormals included) and the sign bit in bit 15.
-__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t w) {
-  return ((w & 0x00070007u) << 9) | ((w & 0x00080008u) << 12);
+// Shared-memory plan for reduction depth K: a 16-row activation buffer (rows padded by 16 B:
+// conflict-free fragment reads), then a ring of stages of R strip records, R the largest power
+// of two with R records <= 24 KB, the stage count a multiple of the consumer warps.
+struct MoePlan {
+  int xrow, x_off, ring_off, run, stage_bytes, nstage, smem;
+};
+
+inline MoePlan moe_plan(int K) {
+  MoePlan m{};
+  const int rec = (K / MOE_GROUP) * 272;
+  m.xrow = K + 16;
+  m.x_off = MOE_HDR;
+  m.ring_off = (m.x_off + MOE_BLOCK * m.xrow + 127) & ~127;
+  m.run = 1;
+  while (2 * m.run * rec <= 24 * 1024) m.run *= 2;
+  m.stage_bytes = (m.run * rec + 127) & ~127;
+  const int xch = MOE_PAIRS * MOE_XCH;
+  m.nstage = std::min(MOE_MAX_STAGES, (MOE_SMEM_CAP - m.ring_off - xch) / m.stage_bytes) / MOE_PAIRS * MOE_PAIRS;
+  m.smem = m.ring_off + m.nstage * m.stage_bytes + xch;
+  return m;
 }
 
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
+// The four bytes of w, each two e2m1 codes (low nibble first), -> four f16x2, exactly.
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t& d0, uint32_t& d1, uint32_t& d2,
+                                                uint32_t& d3) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3) : "r"(w));
 }
 
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
@@ -93,19 +117,53 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
   return d;
 }
 
-// f16 bits of 2^x for an integer x (subnormal below 2^-14, 0 below 2^-24, capped at 2^15).
-__device__ __forceinline__ uint32_t pow2_f16_bits(int x) {
-  const int e = x + 15;
-  if (e >= 31) return 0x7800u;            // 2^15 (not reached: the group exponent never exceeds wref)
-  if (e >= 1) return (uint32_t)e << 10;
-  if (e >= -9) return 1u << (e + 9);
-  return 0u;
+// True on both warps of consumer pair pw iff v is true on every lane of both: the pair's two
+// warps leave their loop together, so neither is left alone at a pair barrier.
+__device__ __forceinline__ bool pair_all(int pw, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, 64, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(1 + pw)
+      : "memory");
+  return r != 0;
 }
 
-// 2^x as fp32 for -149 <= x <= 127 (exact powers of two).
-__device__ __forceinline__ float pow2_f32(int x) {
-  if (x >= -126) return __int_as_float((x + 127) << 23);
-  return __int_as_float(1 << (x + 149));
+// One 16-row strip against the block's NT x 8 activation rows, groups [g0, g1): per 32-K group, the
+// lane's 8 code bytes -> 8 f16x2 A registers, two MMAs from zero, and the group's sums scaled
+// by 2^(s - 127) (fp32 bits s << 23; E8M0 0 gives 0) into tot. tot[nt][0..1]: row g,
+// tot[nt][2..3]: row g + 8, block rows 8 nt + 2 t and + 1.
+template <int NT>
+__device__ __forceinline__ void strip_dot(const char* stg, const char* X, int xrow, int NG, int g0, int g1,
+                                          int lane, float (&tot)[2][4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* sc0 = reinterpret_cast<const uint8_t*>(stg + NG * 256) + g * NG;
+  const uint8_t* sc1 = sc0 + 8 * NG;
+  const char* xb = X + g * xrow + 2 * t;
+#pragma unroll 2
+  for (int gi = g0; gi < g1; ++gi) {
+    const uint2 wv = *reinterpret_cast<const uint2*>(stg + gi * 256 + lane * 8);
+    const float m0 = __uint_as_float((uint32_t)sc0[gi] << 23), m1 = __uint_as_float((uint32_t)sc1[gi] << 23);
+    uint32_t a[2][4];
+    e2m1x8_to_f16x2(wv.x, a[0][0], a[0][1], a[0][2], a[0][3]);
+    e2m1x8_to_f16x2(wv.y, a[1][0], a[1][1], a[1][2], a[1][3]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const char* xr = xb + 8 * nt * xrow + gi * MOE_GROUP;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t b0 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(xr + 16 * h));
+        const uint32_t b1 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(xr + 16 * h + 8));
+        b200::mma_f16_16816(c, a[h][0], a[h][1], a[h][2], a[h][3], b0, b1);
+      }
+      tot[nt][0] = fmaf(m0, c[0], tot[nt][0]);
+      tot[nt][1] = fmaf(m0, c[1], tot[nt][1]);
+      tot[nt][2] = fmaf(m1, c[2], tot[nt][2]);
+      tot[nt][3] = fmaf(m1, c[3], tot[nt][3]);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) {
@@ -117,13 +175,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
   int* rowid = reinterpret_cast<int*>(xempty + 1);   // [16] the block's row ids (-1: padding)
   char* ring = sm + p.ring_off;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NS = p.N / 16, NG = p.K / MOE_GROUP;
-  const int wbytes = NG * 256, sbytes = NG * 16;
+  const int NS = p.N / 16, NG = p.K / MOE_GROUP, rec = NG * 272;
+  const int NR = (NS + p.run - 1) / p.run;           // runs (units) per block
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.nstage; ++i) {
       b200::mbar_init(&full[i], 1);
-      b200::mbar_init(&empty[i], 1);
+      b200::mbar_init(&empty[i], 2);      // both warps of the pair
     }
     b200::mbar_init(xfull, 1);
     b200::mbar_init(xempty, MOE_NC);
@@ -134,7 +192,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
 
   // the units of the live blocks, split evenly over the CTAs
   const int live = min(max(p.npad[0], 0), p.em) / MOE_BLOCK;
-  const long long units = (long long)live * NS;
+  const long long units = (long long)live * NR;
   const int u0 = (int)(units * blockIdx.x / gridDim.x), u1 = (int)(units * (blockIdx.x + 1) / gridDim.x);
 
   if (warp == 0) {
@@ -142,44 +200,85 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     if (lane == 0) {
       const uint64_t pol = b200::l2_policy_evict_first();
       bool ok = true;
-      int q = 0, nb = 0, cur_b = -1;
-      for (int u = u0; u < u1 && ok; ++u) {
-        const int b = u / NS, s = u - b * NS;
-        const int e = p.eids[b];
+      int q = 0, nb = 0, pend = -1, b = u0 / NR, s = u0 - b * NR, e = -1, cur_b = -1;
+      // block blk's row ids and activation rows into the buffer (its previous user released it)
+      auto load_x = [&](int blk) {
+        int ids[MOE_BLOCK], nlive = 0;
+#pragma unroll
+        for (int r = 0; r < MOE_BLOCK; ++r) {
+          const int id = p.sorted[blk * MOE_BLOCK + r];
+          ids[r] = (id >= 0 && id < p.mtk) ? id : -1;
+          rowid[r] = ids[r];
+          nlive += ids[r] >= 0;
+        }
+        char* X = sm + p.x_off;
+        b200::mbar_arrive_expect_tx(xfull, (uint32_t)(nlive * p.K));
+#pragma unroll
+        for (int r = 0; r < MOE_BLOCK; ++r)
+          if (ids[r] >= 0)
+            b200::bulk_g2s(X + r * p.xrow, p.qx + (long long)(ids[r] / p.top_k) * p.K, (uint32_t)p.K, xfull);
+        ++nb;
+      };
+      // A new block's weights stream on while the consumers finish the previous block; its
+      // activation rows go as soon as they release the buffer (checked inside every slot wait,
+      // so the producer never waits on a slot whose consumer waits for those rows).
+      auto service = [&]() {
+        if (pend >= 0 && b200::mbar_test_wait(xempty, (nb - 1) & 1)) {
+          load_x(pend);
+          pend = -1;
+        }
+      };
+      for (int u = u0; u < u1; ++u, ++s) {
+        if (s == NR) {
+          s = 0;
+          ++b;
+        }
+        if (b != cur_b) {
+          cur_b = b;
+          e = p.eids[b];
+          if (e < 0) continue;
+          if (pend >= 0) {                  // every unit before it is issued: this wait ends
+            if (!b200::mbar_wait_bounded(xempty, (nb - 1) & 1, deadline)) {
+              ok = false;
+              break;
+            }
+            load_x(pend);
+            pend = -1;
+          }
+          if (nb == 0) {
+            load_x(b);
+          } else {
+            pend = b;
+            service();
+          }
+        }
         if (e < 0) continue;
-        if (b != cur_b) {                   // a new block: its activation rows, once released
-          if (nb >= 1 && !b200::mbar_wait_bounded(xempty, (nb - 1) & 1, deadline)) {
+        const int slot = q % p.nstage;
+        if (q >= p.nstage) {
+          const uint32_t par = ((q / p.nstage) - 1) & 1;
+          uint32_t n = 0;
+          bool got;
+          while (!(got = b200::mbar_try_wait(&empty[slot], par))) {
+            service();
+            if ((++n & 15u) == 0 && b200::globaltimer_ns() > deadline) break;
+          }
+          if (!got) {
             ok = false;
             break;
           }
-          int ids[MOE_BLOCK], nlive = 0;
-#pragma unroll
-          for (int r = 0; r < MOE_BLOCK; ++r) {
-            const int id = p.sorted[b * MOE_BLOCK + r];
-            ids[r] = (id >= 0 && id < p.mtk) ? id : -1;
-            rowid[r] = ids[r];
-            nlive += ids[r] >= 0;
-          }
-          char* X = sm + p.x_off;
-          b200::mbar_arrive_expect_tx(xfull, (uint32_t)(nlive * p.K));
-#pragma unroll
-          for (int r = 0; r < MOE_BLOCK; ++r)
-            if (ids[r] >= 0)
-              b200::bulk_g2s(X + r * p.xrow, p.qx + (long long)(ids[r] / p.top_k) * p.K, (uint32_t)p.K, xfull);
-          cur_b = b;
-          ++nb;
-        }
-        const int slot = q % p.nstage;
-        if (q >= p.nstage && !b200::mbar_wait_bounded(&empty[slot], ((q / p.nstage) - 1) & 1, deadline)) {
-          ok = false;
-          break;
         }
         char* dst = ring + slot * p.stage_bytes;
-        const long long strip = (long long)e * NS + s;
-        b200::mbar_arrive_expect_tx(&full[slot], (uint32_t)(wbytes + sbytes));
-        b200::bulk_g2s_stream(dst, p.wq + strip * wbytes, (uint32_t)wbytes, &full[slot], pol);
-        b200::bulk_g2s(dst + wbytes, p.ws + strip * sbytes, (uint32_t)sbytes, &full[slot]);
+        const int s0 = s * p.run, ns = min(p.run, NS - s0);
+        const uint32_t bytes = (uint32_t)(ns * rec);
+        b200::mbar_arrive_expect_tx(&full[slot], bytes);
+        b200::bulk_g2s_stream(dst, p.wq + ((long long)e * NS + s0) * rec, bytes, &full[slot], pol);
         ++q;
+      }
+      if (ok && pend >= 0) {
+        if (b200::mbar_wait_bounded(xempty, (nb - 1) & 1, deadline))
+          load_x(pend);
+        else
+          ok = false;
       }
       if (!ok) atomicExch(&g_moe_err, 1);
       // never leave with copies in flight: the last use of every slot must have landed
@@ -191,80 +290,91 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     return;
   }
 
-  // ---------------- consumers: unit q of the CTA's sequence goes to warp q % 4 ----------------
-  const int cw = warp - 1, g = lane >> 2, t = lane & 3;
+  // ---- consumers: unit q of the CTA's sequence goes to warp pair q % 8; the pair's first warp
+  // takes the strip's first half of the 32-K groups, the second warp the rest, and hands its
+  // partial sums to the first through shared memory (two buffers, one pair barrier per strip)
+  const int cw = warp - 1, pw = cw >> 1, half = cw & 1, g = lane >> 2, t = lane & 3;
+  float* xch = reinterpret_cast<float*>(sm + p.xch_off + pw * MOE_XCH);
   bool ok = true;
-  int q = 0, nb = 0, cur_b = -1, ntile = 2;
+  int q = 0, nb = 0, ntile = 2, b = u0 / NR, s = u0 - b * NR, e = -1, cur_b = -1;
   int rid[MOE_BLOCK / 4];                   // this lane's epilogue rows: 8 nt + 2 t + c
-  for (int u = u0; u < u1 && ok; ++u) {
-    const int b = u / NS, s = u - b * NS;
-    const int e = p.eids[b];
-    if (e < 0) continue;
+  int xq = 0;                               // strips exchanged so far (buffer parity)
+  float rs = 0.f;                           // lane r < 16: block row r's token scale x routed weight
+  for (int u = u0; u < u1; ++u, ++s) {
+    if (s == NR) {
+      s = 0;
+      ++b;
+    }
     if (b != cur_b) {
+      cur_b = b;
+      e = p.eids[b];
+      if (e < 0) continue;
       if (nb > 0) {                          // done with the previous block's activation
         __syncwarp();
         if (lane == 0) b200::mbar_arrive(xempty);
       }
-      ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(xfull, nb & 1, deadline));
+      ok = pair_all(pw, b200::mbar_wait_bounded(xfull, nb & 1, deadline));
       if (!ok) break;
       ntile = 1;
       for (int r = 8; r < MOE_BLOCK; ++r) ntile = rowid[r] >= 0 ? 2 : ntile;
 #pragma unroll
       for (int j = 0; j < MOE_BLOCK / 4; ++j) rid[j] = rowid[8 * (j >> 1) + 2 * t + (j & 1)];
-      cur_b = b;
+      rs = 0.f;
+      const int my = rowid[lane & 15];
+      if (lane < MOE_BLOCK && my >= 0) {
+        rs = p.xs[my / p.top_k];
+        if (p.tw != nullptr) rs *= p.tw[my];
+      }
       ++nb;
     }
+    if (e < 0) continue;
     const int myq = q++;
-    if ((myq & (MOE_NC - 1)) != cw) continue;
+    if ((myq & (MOE_PAIRS - 1)) != pw) continue;
     const int slot = myq % p.nstage;
-    ok = __all_sync(0xffffffffu, b200::mbar_wait_bounded(&full[slot], (myq / p.nstage) & 1, deadline));
+    ok = pair_all(pw, b200::mbar_wait_bounded(&full[slot], (myq / p.nstage) & 1, deadline));
     if (!ok) break;
-    const int n0 = s * 16;
-    const int wr0 = p.wref[(long long)e * p.N + n0 + g], wr1 = p.wref[(long long)e * p.N + n0 + g + 8];
-    const char* stg = ring + slot * p.stage_bytes;
-    const uint8_t* sc = reinterpret_cast<const uint8_t*>(stg + wbytes);
-    const char* X = sm + p.x_off;
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 2
-    for (int gi = 0; gi < NG; ++gi) {
-      const uint2 wv = *reinterpret_cast<const uint2*>(stg + gi * 256 + lane * 8);
-      const uint32_t h0 = pow2_f16_bits(14 - (wr0 - (int)sc[gi * 16 + g]));
-      const uint32_t h1 = pow2_f16_bits(14 - (wr1 - (int)sc[gi * 16 + g + 8]));
-      const uint32_t s0 = h0 | (h0 << 16), s1 = h1 | (h1 << 16);
+    const int s0 = s * p.run, ns = min(p.run, NS - s0);
+    float sx[2][2];                          // block rows 8 nt + 2 t + c
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t wd = h ? wv.y : wv.x;
-        const uint32_t a0 = hmul2_u32(e2m1x2_to_f16x2(wd), s0);
-        const uint32_t a1 = hmul2_u32(e2m1x2_to_f16x2(wd >> 4), s1);
-        const uint32_t a2 = hmul2_u32(e2m1x2_to_f16x2(wd >> 8), s0);
-        const uint32_t a3 = hmul2_u32(e2m1x2_to_f16x2(wd >> 12), s1);
-        const int k = gi * MOE_GROUP + 16 * h + 2 * t;
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          if (nt >= ntile) break;
-          const char* xr = X + (8 * nt + g) * p.xrow + k;
-          const uint32_t b0 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(xr));
-          const uint32_t b1 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(xr + 8));
-          b200::mma_f16_16816(acc[nt], a0, a1, a2, a3, b0, b1);
-        }
+      for (int c = 0; c < 2; ++c) sx[nt][c] = __shfl_sync(0xffffffffu, rs, 8 * nt + 2 * t + c);
+    const int gsplit = NG / 2, ga = half ? gsplit : 0, gb = half ? NG : gsplit;
+    for (int j = 0; j < ns; ++j) {
+      const char* stg = ring + slot * p.stage_bytes + j * rec;
+      float tot[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if (ntile == 1)
+        strip_dot<1>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
+      else
+        strip_dot<2>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
+      if (j == ns - 1) {                     // this warp is done with the stage
+        __syncwarp();
+        if (lane == 0) b200::mbar_arrive(&empty[slot]);
       }
-    }
-    __syncwarp();
-    if (lane == 0) b200::mbar_arrive(&empty[slot]);
-    // epilogue: weight rows n0 + g (c0, c1) and n0 + g + 8 (c2, c3); block rows 8 nt + 2 t (+1)
-    const float f0 = pow2_f32(wr0 - 127), f1 = pow2_f32(wr1 - 127);
+      float4* xb = reinterpret_cast<float4*>(xch + (xq & 1) * (32 * 8)) + 2 * lane;
+      if (half) {
+        xb[0] = make_float4(tot[0][0], tot[0][1], tot[0][2], tot[0][3]);
+        xb[1] = make_float4(tot[1][0], tot[1][1], tot[1][2], tot[1][3]);
+      }
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + pw) : "memory");
+      ++xq;
+      if (half) continue;
+      const float4 o0 = xb[0], o1 = xb[1];
+      tot[0][0] += o0.x; tot[0][1] += o0.y; tot[0][2] += o0.z; tot[0][3] += o0.w;
+      tot[1][0] += o1.x; tot[1][1] += o1.y; tot[1][2] += o1.z; tot[1][3] += o1.w;
+      // epilogue: weight rows n0 + g (c0, c1) and n0 + g + 8 (c2, c3); block rows 8 nt + 2 t (+1)
+      const int n0 = (s0 + j) * 16;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      if (nt >= ntile) break;
+      for (int nt = 0; nt < 2; ++nt) {
+        if (nt >= ntile) break;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int id = rid[2 * nt + c];
-        if (id < 0) continue;
-        float sx = p.xs[id / p.top_k];
-        if (p.tw != nullptr) sx *= p.tw[id];
-        __nv_bfloat16* yr = p.y + (long long)id * p.N + n0 + g;
-        yr[0] = __float2bfloat16_rn(acc[nt][c] * f0 * sx);
-        yr[8] = __float2bfloat16_rn(acc[nt][2 + c] * f1 * sx);
+        for (int c = 0; c < 2; ++c) {
+          const int id = rid[2 * nt + c];
+          if (id < 0) continue;
+          __nv_bfloat16* yr = p.y + (long long)id * p.N + n0 + g;
+          yr[0] = __float2bfloat16_rn(tot[nt][c] * sx[nt][c]);
+          yr[8] = __float2bfloat16_rn(tot[nt][2 + c] * sx[nt][c]);
+        }
       }
     }
   }
@@ -288,46 +398,39 @@ int g_moe_last_rc = 0;
 extern "C" {
 
 // Bytes of dynamic shared memory the grouped GEMM needs for reduction depth K, or -1 when K
-// does not fit (the ring needs a multiple of 4 stages, at least 4, beside the activation
+// does not fit (the ring needs at least one stage per consumer warp beside the activation
 // buffer of 16 rows).
 int b200_moe_gemm_smem_bytes(int K) {
-  if (K <= 0 || K % MOE_GROUP) return -1;
-  const int xrow = K + 16;                                   // padded: conflict-free row reads
-  const int x_off = MOE_HDR;
-  const int ring_off = (x_off + MOE_BLOCK * xrow + 127) & ~127;
-  const int stage = ((K / MOE_GROUP) * (256 + 16) + 127) & ~127;
-  const int nstage = std::min(MOE_MAX_STAGES, (MOE_SMEM_CAP - ring_off) / stage) / MOE_NC * MOE_NC;
-  if (nstage < MOE_NC) return -1;
-  return ring_off + nstage * stage;
+  if (K <= 0 || K % MOE_GROUP || K > 32768) return -1;
+  const MoePlan m = moe_plan(K);
+  return m.nstage < MOE_PAIRS ? -1 : m.smem;
 }
 
 // r4d_gemm_moe_mxfp4a8_nt_b16 (the closed kernel's ABI, bound with ctypes by the reference's
 // MoE layer, r4d_mxfp4_moe.py.lru.diff L454-500; argument order as tests/k1/moe_ref_harness.py
-// passes it): qx e4m3 [tokens, K], x_scale fp32 [tokens], wq / ws / wref in the B200 packed
-// layouts above (indexed by expert_ids: the hot call passes the resident slots' copies, the
-// cold call the full tensors), c bf16 [mtk, N], sorted_ids int32 [em], expert_ids int32
+// passes it): qx e4m3 [tokens, K], x_scale fp32 [tokens], wq in the B200 packed layout above
+// (indexed by expert_ids: the hot call passes the resident slots' copies, the cold call the
+// full tensors; ws and wref are accepted and not read), c bf16 [mtk, N], sorted_ids int32 [em], expert_ids int32
 // [em / 16], num_post_pad int32 [1] (read on the device), topk_weights fp32 [mtk] or 0.
 // wv / sk / npw are the gfx1201 launch knobs: accepted (the Python wrapper checks them as the
 // reference does) and ignored. Returns nothing, like the reference; the status of the last
 // call is r4d_gemm_moe_mxfp4a8_nt_b16_last_error(): 0, -1 em < 16 / mtk < 0 / top_k < 1,
-// -2 N % 16, -3 K % 32 or K too deep for shared memory, -10 misaligned pointer, else a CUDA
+// -2 N % 16, -3 K % 32 or K too deep for shared memory, -10 misaligned qx / wq, else a CUDA
 // error.
 void r4d_gemm_moe_mxfp4a8_nt_b16(long qx, long x_scale, long wq, long ws, long wref, long c, long sorted_ids,
                                  long expert_ids, long num_post_pad, long topk_weights, int em, int mtk,
                                  int top_k, int K, int N, int wv, int sk, int npw, long stream) {
-  (void)wv; (void)sk; (void)npw;
+  (void)ws; (void)wref; (void)wv; (void)sk; (void)npw;
   if (em < MOE_BLOCK || mtk < 0 || top_k < 1) { g_moe_last_rc = -1; return; }
   if (N <= 0 || N % 16) { g_moe_last_rc = -2; return; }
   const int smem = b200_moe_gemm_smem_bytes(K);
   if (smem < 0) { g_moe_last_rc = -3; return; }
-  if ((qx & 15) || (wq & 15) || (ws & 15)) { g_moe_last_rc = -10; return; }
+  if ((qx & 15) || (wq & 15)) { g_moe_last_rc = -10; return; }
   if (mtk == 0) { g_moe_last_rc = 0; return; }
   MoeParams p{};
   p.qx = reinterpret_cast<const uint8_t*>(qx);
   p.xs = reinterpret_cast<const float*>(x_scale);
   p.wq = reinterpret_cast<const uint8_t*>(wq);
-  p.ws = reinterpret_cast<const uint8_t*>(ws);
-  p.wref = reinterpret_cast<const uint8_t*>(wref);
   p.y = reinterpret_cast<__nv_bfloat16*>(c);
   p.sorted = reinterpret_cast<const int*>(sorted_ids);
   p.eids = reinterpret_cast<const int*>(expert_ids);
@@ -338,11 +441,14 @@ void r4d_gemm_moe_mxfp4a8_nt_b16(long qx, long x_scale, long wq, long ws, long w
   p.top_k = top_k;
   p.K = K;
   p.N = N;
-  p.xrow = K + 16;
-  p.x_off = MOE_HDR;
-  p.ring_off = (p.x_off + MOE_BLOCK * p.xrow + 127) & ~127;
-  p.stage_bytes = ((K / MOE_GROUP) * (256 + 16) + 127) & ~127;
-  p.nstage = std::min(MOE_MAX_STAGES, (MOE_SMEM_CAP - p.ring_off) / p.stage_bytes) / MOE_NC * MOE_NC;
+  const MoePlan m = moe_plan(K);
+  p.xrow = m.xrow;
+  p.x_off = m.x_off;
+  p.ring_off = m.ring_off;
+  p.run = m.run;
+  p.stage_bytes = m.stage_bytes;
+  p.nstage = m.nstage;
+  p.xch_off = m.ring_off + m.nstage * m.stage_bytes;
   static bool smem_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

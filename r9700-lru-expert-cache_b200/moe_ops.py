@@ -48,9 +48,9 @@ MOE_GROUP = 32       # K per E8M0 exponent (r4d_gemm_moe_mxfp4a8_nt_b16_group)
 
 
 def _pack_index(device):
-    """For lane l = 4 g + t of a 32-K group, word h, nibble pair p and element j (0: low nibble
-    pair position, 1: high): the (row in the 16-row strip, k in the group) the code comes from,
-    and its bit position in the lane's 8 bytes (word h at byte 4 h)."""
+    """For lane l = 4 g + t of a 32-K group, k-half h, A register p and element j (0: low
+    nibble, 1: high): the (row in the 16-row strip, k in the group) the code comes from, and its
+    bit position in the lane's 8 bytes (byte 4 h + p, element j in nibble j)."""
     lane = torch.arange(32, device=device).view(32, 1, 1, 1)
     h = torch.arange(2, device=device).view(1, 2, 1, 1)
     p = torch.arange(4, device=device).view(1, 1, 4, 1)
@@ -58,7 +58,7 @@ def _pack_index(device):
     g, t = lane >> 2, lane & 3
     row = (g + 8 * (p & 1)).expand(32, 2, 4, 2)
     k = (16 * h + 2 * t + 8 * (p >> 1) + j).expand(32, 2, 4, 2)
-    shift = (32 * h + 4 * p + 16 * j).expand(32, 2, 4, 2)
+    shift = (32 * h + 8 * p + 4 * j).expand(32, 2, 4, 2)
     return row, k, shift
 
 
@@ -69,8 +69,12 @@ def pack_mxfp4_moe(w: torch.Tensor, scales: torch.Tensor):
     w uint8 [E, N, K/2]: byte j of a row holds the e2m1 code of k = 2 j in its low nibble and of
     k = 2 j + 1 in its high nibble (the checkpoint order the reference permutes,
     r4d_mxfp4_moe.py.lru.diff _permute_moe_inplace); scales uint8 [E, N, K/32] E8M0.
-    Returns (wq uint8 [E, N/16, K/32, 256], ws uint8 [E, N/16, K/32, 16], wref uint8 [E, N]),
-    wref being each row's largest exponent (the reference's w*_wref = s.max(dim=2))."""
+    Returns (wq uint8 [E, N/16, 272 K/32], ws, wref): wq holds one record per 16-row strip --
+    the codes in mma.sync fragment order [K/32][32 lanes][8 B], then the strip's exponents
+    [16 rows][K/32] -- so that a run of strips is one contiguous copy; ws (the scales viewed by
+    strip, [E, N/16, 16, K/32]) and wref (each row's largest exponent, the reference's
+    w*_wref = s.max(dim=2)) complete the reference's argument list and are not read by the
+    kernel."""
     E, N, K2 = w.shape
     K = 2 * K2
     if w.dtype != torch.uint8 or scales.dtype != torch.uint8 or scales.shape != (E, N, K // MOE_GROUP):
@@ -79,33 +83,35 @@ def pack_mxfp4_moe(w: torch.Tensor, scales: torch.Tensor):
         raise ValueError("pack_mxfp4_moe: N % 16 == 0 and K % 32 == 0 are required")
     NS, G = N // 16, K // MOE_GROUP
     row, k, shift = _pack_index(w.device)
-    wq = torch.empty(E, NS, G, 256, dtype=torch.uint8, device=w.device)
+    wq = torch.empty(E, NS, G * 272, dtype=torch.uint8, device=w.device)
     for e in range(E):                       # one expert at a time bounds the temporaries
         codes = torch.stack((w[e] & 0xF, w[e] >> 4), dim=-1).reshape(NS, 16, G, MOE_GROUP)
         codes = codes.permute(0, 2, 1, 3)                                   # [NS, G, 16, 32]
         picked = codes[:, :, row, k].to(torch.int64)                        # [NS, G, 32, 2, 4, 2]
         word64 = (picked << shift).sum(dim=(-1, -2, -3))                    # [NS, G, 32]
         b = torch.stack([(word64 >> (8 * i)) & 0xFF for i in range(8)], dim=-1)
-        wq[e] = b.to(torch.uint8).reshape(NS, G, 256)
-    ws = scales.reshape(E, NS, 16, G).permute(0, 1, 3, 2).contiguous()
+        wq[e, :, :G * 256] = b.to(torch.uint8).reshape(NS, G * 256)
+    ws = scales.reshape(E, NS, 16, G).contiguous()
+    wq[:, :, G * 256:] = ws.reshape(E, NS, 16 * G)
     wref = scales.max(dim=2).values.contiguous()
     return wq, ws, wref
 
 
 @torch.no_grad()
-def unpack_mxfp4_moe(wq: torch.Tensor, ws: torch.Tensor):
-    """The inverse of pack_mxfp4_moe's code and scale regrouping: (w [E, N, K/2], scales
-    [E, N, K/32]) in checkpoint order."""
-    E, NS, G, _ = wq.shape
+def unpack_mxfp4_moe(wq: torch.Tensor):
+    """The inverse of pack_mxfp4_moe's records: (w [E, N, K/2], scales [E, N, K/32]) in
+    checkpoint order."""
+    E, NS, R = wq.shape
+    G = R // 272
     row, k, shift = _pack_index(wq.device)
-    b = wq.reshape(E, NS, G, 32, 8).to(torch.int64)
+    b = wq[:, :, :G * 256].reshape(E, NS, G, 32, 8).to(torch.int64)
     word64 = sum(b[..., i] << (8 * i) for i in range(8))                    # [E, NS, G, 32]
     codes = torch.empty(E, NS, G, 16, MOE_GROUP, dtype=torch.uint8, device=wq.device)
     vals = ((word64.view(E, NS, G, 32, 1, 1, 1) >> shift) & 0xF).to(torch.uint8)
     codes[:, :, :, row, k] = vals
     codes = codes.permute(0, 1, 3, 2, 4).reshape(E, NS * 16, G * MOE_GROUP)
     w = (codes[..., 0::2] | (codes[..., 1::2] << 4)).contiguous()
-    scales = ws.permute(0, 1, 3, 2).reshape(E, NS * 16, G).contiguous()
+    scales = wq[:, :, G * 256:].reshape(E, NS * 16, G).contiguous()
     return w, scales
 
 
@@ -124,20 +130,23 @@ def mxfp4_moe_gemm_into(y: torch.Tensor, qx: torch.Tensor, x_scale: torch.Tensor
                         wv: int = 1, sk: int = 1, npw: int = 1) -> None:
     """y[i, :] for every row i the aligned blocks name (the rows of a block share its expert):
     bf16(topk_weights[i] * x_scale[i // top_k] * qx[i // top_k] . W_e); other rows untouched.
-    qx e4m3 [tokens, K], x_scale fp32 [tokens] (or [tokens, 1]); wq / ws / wref from
-    pack_mxfp4_moe (or the hot experts' compact copies indexed by slot); y bf16 [mtk, N]."""
+    qx e4m3 [tokens, K], x_scale fp32 [tokens] (or [tokens, 1]); wq from pack_mxfp4_moe (or the
+    hot experts' compact copies indexed by slot); ws / wref are the reference's remaining
+    arguments (any CUDA tensors: the kernel reads codes and exponents from wq); y bf16
+    [mtk, N]."""
     _lib.require_cuda("r4d_mxfp4_moe_gemm", y, qx, x_scale, wq, ws, wref, sorted_ids, expert_ids,
                       num_post_pad, topk_weights)
     K = qx.shape[1]
-    E, NS, G, _ = wq.shape
+    E, NS, R = wq.shape
+    G = R // 272
     N = NS * 16
     em = sorted_ids.numel()
     if y.shape != (mtk, N) or y.dtype != torch.bfloat16 or not y.is_contiguous():
         raise ValueError(f"r4d_mxfp4_moe_gemm: y must be contiguous bf16 [{mtk}, {N}]")
     if G * MOE_GROUP != K or qx.dtype != torch.float8_e4m3fn or not qx.is_contiguous():
         raise ValueError("r4d_mxfp4_moe_gemm: qx must be contiguous e4m3 [tokens, K] matching the pack")
-    if ws.shape != (E, NS, G, 16) or wref.shape != (E, N):
-        raise ValueError("r4d_mxfp4_moe_gemm: ws / wref do not match wq")
+    if R % 272 or wq.dtype != torch.uint8 or not wq.is_contiguous():
+        raise ValueError("r4d_mxfp4_moe_gemm: wq must be a contiguous uint8 [E, N/16, 272 K/32] pack")
     for t, name in ((sorted_ids, "sorted_ids"), (expert_ids, "expert_ids"), (num_post_pad, "num_post_pad")):
         if t.dtype != torch.int32 or not t.is_contiguous():
             raise ValueError(f"r4d_mxfp4_moe_gemm: {name} must be contiguous int32")

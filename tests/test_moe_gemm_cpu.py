@@ -22,15 +22,16 @@ def test_pack_round_trip(E, N, K):
     w = torch.randint(0, 256, (E, N, K // 2), generator=g, dtype=torch.uint8)
     s = torch.randint(100, 140, (E, N, K // 32), generator=g, dtype=torch.uint8)
     wq, ws, wref = MO.pack_mxfp4_moe(w, s)
-    assert wq.shape == (E, N // 16, K // 32, 256) and ws.shape == (E, N // 16, K // 32, 16)
+    assert wq.shape == (E, N // 16, (K // 32) * 272) and ws.shape == (E, N // 16, 16, K // 32)
     assert torch.equal(wref, s.max(dim=2).values)
-    w2, s2 = MO.unpack_mxfp4_moe(wq, ws)
+    assert torch.equal(wq[:, :, (K // 32) * 256:].reshape(E, N, K // 32), s)     # exponents in the record
+    w2, s2 = MO.unpack_mxfp4_moe(wq)
     assert torch.equal(w2, w) and torch.equal(s2, s)
 
 
 def test_pack_fragment_positions():
-    """Code of (row r, k) lands in lane 4 (r % 8) + (k % 8) // 2 of its group, word k // 16,
-    nibble pair 2 ((k % 16) // 8) + r // 8, element k % 2."""
+    """Code of (row r, k) lands in lane 4 (r % 8) + (k % 8) // 2 of its group, byte
+    4 (k // 16) + 2 ((k % 16) // 8) + r // 8, nibble k % 2."""
     for r, k in ((1, 27), (9, 0), (15, 31), (0, 17), (8, 12)):
         codes = torch.zeros(16, 32, dtype=torch.uint8)
         codes[r, k] = 0xB
@@ -38,10 +39,10 @@ def test_pack_fragment_positions():
         wq, _, _ = MO.pack_mxfp4_moe(w, torch.full((1, 16, 1), 127, dtype=torch.uint8))
         lane = 4 * (r % 8) + (k % 8) // 2
         h, pair, j = k // 16, 2 * ((k % 16) // 8) + r // 8, k % 2
-        b = wq[0, 0, 0].view(32, 8)[lane]
+        b = wq[0, 0, :256].view(32, 8)[lane]
         word = sum(int(b[4 * h + i]) << (8 * i) for i in range(4))
-        assert word == 0xB << (4 * pair + 16 * j), (r, k, hex(word))
-        assert int(wq[0, 0, 0].view(torch.int64).ne(0).sum()) == 1
+        assert word == 0xB << (8 * pair + 4 * j), (r, k, hex(word))
+        assert int(wq[0, 0, :256].view(torch.int64).ne(0).sum()) == 1
 
 
 def test_dequant_and_align_hand_cases():
