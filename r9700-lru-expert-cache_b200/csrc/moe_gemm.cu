@@ -56,12 +56,12 @@ namespace {
 constexpr int MOE_BLOCK = 16;             // rows per aligned block (moe_align block size)
 constexpr int MOE_GROUP = 32;             // K per E8M0 exponent
 constexpr int MOE_NC = 16;                // consumer warps
-constexpr int MOE_PAIRS = MOE_NC / 2;     // ... in pairs: one unit per pair, K split between them
+constexpr int MOE_OCT = 8;                // ... in teams (team_plan); the ring is a multiple of 8
 constexpr int MOE_THREADS = 32 * (1 + MOE_NC);
 constexpr int MOE_MAX_STAGES = 32;
 constexpr int MOE_SMEM_CAP = 227 * 1024;
 constexpr int MOE_HDR = 640;              // barriers (66 x 8 B) and the block's row ids (64 B)
-constexpr int MOE_XCH = 2 * 32 * 8 * 4;   // per pair: two buffers of 8 partial sums per lane
+constexpr int MOE_XCH = MOE_NC * 8 * 32 * 4;    // 8 partial sums per lane of each consumer warp
 constexpr uint64_t MOE_WAIT_NS = 2000000000ull;
 
 __device__ int g_moe_err = 0;             // 1 = a pipeline wait timed out
@@ -77,7 +77,7 @@ struct MoeParams {
   const float* tw;         // [mtk] or nullptr
   int em, mtk, top_k, K, N;
   int nstage, stage_bytes, xrow, x_off, ring_off, run;   // run = R strips per unit
-  int xch_off;                                            // the pairs' exchange buffers
+  int xch_off;                                            // the teams' exchange buffers
 };
 
 // Shared-memory plan for reduction depth K: a 16-row activation buffer (rows padded by 16 B:
@@ -96,8 +96,8 @@ inline MoePlan moe_plan(int K) {
   m.run = 1;
   while (2 * m.run * rec <= 24 * 1024) m.run *= 2;
   m.stage_bytes = (m.run * rec + 127) & ~127;
-  const int xch = MOE_PAIRS * MOE_XCH;
-  m.nstage = std::min(MOE_MAX_STAGES, (MOE_SMEM_CAP - m.ring_off - xch) / m.stage_bytes) / MOE_PAIRS * MOE_PAIRS;
+  const int xch = MOE_XCH;
+  m.nstage = std::min(MOE_MAX_STAGES, (MOE_SMEM_CAP - m.ring_off - xch) / m.stage_bytes) / MOE_OCT * MOE_OCT;
   m.smem = m.ring_off + m.nstage * m.stage_bytes + xch;
   return m;
 }
@@ -117,17 +117,31 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
   return d;
 }
 
-// True on both warps of consumer pair pw iff v is true on every lane of both: the pair's two
-// warps leave their loop together, so neither is left alone at a pair barrier.
-__device__ __forceinline__ bool pair_all(int pw, bool v) {
+// Consumer teams for R strips per unit: a strip of 2 x 32 K (R < 8) is shared by two warps
+// (wps = 2), and a team holds R such pairs, at least one; with R >= 8 every warp takes whole
+// strips (wps = 1) in teams of 8 (16 for R >= 16). TS warps per team, NT = 16 / TS teams (a
+// divisor of the ring's stage count, which is a multiple of 8).
+__host__ __device__ __forceinline__ void team_plan(int run, int& TS, int& NT, int& wps) {
+  wps = run < MOE_OCT ? 2 : 1;
+  TS = run < MOE_OCT ? 2 * run : (run >= 2 * MOE_OCT ? MOE_NC : MOE_OCT);
+  NT = MOE_NC / TS;
+}
+
+// True on all TS warps of consumer team tm iff v is true on every lane of all of them: the
+// team's warps leave their loop together, so none is left alone at a team barrier (ids 1..8).
+__device__ __forceinline__ bool team_all(int tm, int TS, bool v) {
   uint32_t r;
   asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, 64, q;\n\t"
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)v), "r"(1 + pw)
+      : "r"((uint32_t)v), "r"(1 + tm), "r"(32 * TS)
       : "memory");
   return r != 0;
+}
+
+__device__ __forceinline__ void team_sync(int tm, int TS) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + tm), "r"(32 * TS) : "memory");
 }
 
 // One 16-row strip against the block's NT x 8 activation rows, groups [g0, g1): per 32-K group, the
@@ -179,9 +193,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
   const int NR = (NS + p.run - 1) / p.run;           // runs (units) per block
 
   if (threadIdx.x == 0) {
+    int ts, nt, wps0;
+    team_plan(p.run, ts, nt, wps0);
     for (int i = 0; i < p.nstage; ++i) {
       b200::mbar_init(&full[i], 1);
-      b200::mbar_init(&empty[i], 2);      // both warps of the pair
+      b200::mbar_init(&empty[i], ts);       // every warp of the unit's team
     }
     b200::mbar_init(xfull, 1);
     b200::mbar_init(xempty, MOE_NC);
@@ -290,15 +306,20 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     return;
   }
 
-  // ---- consumers: unit q of the CTA's sequence goes to warp pair q % 8; the pair's first warp
-  // takes the strip's first half of the 32-K groups, the second warp the rest, and hands its
-  // partial sums to the first through shared memory (two buffers, one pair barrier per strip)
-  const int cw = warp - 1, pw = cw >> 1, half = cw & 1, g = lane >> 2, t = lane & 3;
-  float* xch = reinterpret_cast<float*>(sm + p.xch_off + pw * MOE_XCH);
+  // ---- consumers: teams of TS warps (team_plan); unit q of the CTA's sequence goes to team
+  // q % NT. Within a unit the team's warps split the work: with wps = 1 each warp takes whole
+  // strips; with wps = 2 two warps share a strip, each taking half of its 32-K groups, and
+  // their partial sums meet in shared memory, where each of the two reduces and stores half of
+  // the values. (Few large strips per unit: small teams, so that more units are in flight; many
+  // small strips: a strip per warp and no reduction.)
+  int TS, NT, wps;
+  team_plan(p.run, TS, NT, wps);
+  const int cw = warp - 1, tm = cw / TS, wi = cw - tm * TS, g = lane >> 2, t = lane & 3;
+  float* part = reinterpret_cast<float*>(sm + p.xch_off) + tm * TS * 256;   // [TS warps][8 values][32]
+  const int sj = wi / wps, sp = wi - sj * wps;             // this warp's strip in the unit, its part
   bool ok = true;
   int q = 0, nb = 0, ntile = 2, b = u0 / NR, s = u0 - b * NR, e = -1, cur_b = -1;
   int rid[MOE_BLOCK / 4];                   // this lane's epilogue rows: 8 nt + 2 t + c
-  int xq = 0;                               // strips exchanged so far (buffer parity)
   float rs = 0.f;                           // lane r < 16: block row r's token scale x routed weight
   for (int u = u0; u < u1; ++u, ++s) {
     if (s == NR) {
@@ -313,7 +334,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
         __syncwarp();
         if (lane == 0) b200::mbar_arrive(xempty);
       }
-      ok = pair_all(pw, b200::mbar_wait_bounded(xfull, nb & 1, deadline));
+      ok = team_all(tm, TS, b200::mbar_wait_bounded(xfull, nb & 1, deadline));
       if (!ok) break;
       ntile = 1;
       for (int r = 8; r < MOE_BLOCK; ++r) ntile = rowid[r] >= 0 ? 2 : ntile;
@@ -329,9 +350,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     }
     if (e < 0) continue;
     const int myq = q++;
-    if ((myq & (MOE_PAIRS - 1)) != pw) continue;
+    if (myq % NT != tm) continue;
     const int slot = myq % p.nstage;
-    ok = pair_all(pw, b200::mbar_wait_bounded(&full[slot], (myq / p.nstage) & 1, deadline));
+    ok = team_all(tm, TS, b200::mbar_wait_bounded(&full[slot], (myq / p.nstage) & 1, deadline));
     if (!ok) break;
     const int s0 = s * p.run, ns = min(p.run, NS - s0);
     float sx[2][2];                          // block rows 8 nt + 2 t + c
@@ -339,43 +360,61 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int c = 0; c < 2; ++c) sx[nt][c] = __shfl_sync(0xffffffffu, rs, 8 * nt + 2 * t + c);
-    const int gsplit = NG / 2, ga = half ? gsplit : 0, gb = half ? NG : gsplit;
-    for (int j = 0; j < ns; ++j) {
-      const char* stg = ring + slot * p.stage_bytes + j * rec;
-      float tot[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      if (ntile == 1)
-        strip_dot<1>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
-      else
-        strip_dot<2>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
-      if (j == ns - 1) {                     // this warp is done with the stage
-        __syncwarp();
-        if (lane == 0) b200::mbar_arrive(&empty[slot]);
-      }
-      float4* xb = reinterpret_cast<float4*>(xch + (xq & 1) * (32 * 8)) + 2 * lane;
-      if (half) {
-        xb[0] = make_float4(tot[0][0], tot[0][1], tot[0][2], tot[0][3]);
-        xb[1] = make_float4(tot[1][0], tot[1][1], tot[1][2], tot[1][3]);
-      }
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + pw) : "memory");
-      ++xq;
-      if (half) continue;
-      const float4 o0 = xb[0], o1 = xb[1];
-      tot[0][0] += o0.x; tot[0][1] += o0.y; tot[0][2] += o0.z; tot[0][3] += o0.w;
-      tot[1][0] += o1.x; tot[1][1] += o1.y; tot[1][2] += o1.z; tot[1][3] += o1.w;
-      // epilogue: weight rows n0 + g (c0, c1) and n0 + g + 8 (c2, c3); block rows 8 nt + 2 t (+1)
-      const int n0 = (s0 + j) * 16;
+    if (wps == 1) {
+      // whole strips per warp: compute, then store straight from the registers
+      for (int j = wi; j < ns; j += TS) {
+        const char* stg = ring + slot * p.stage_bytes + j * rec;
+        float tot[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        if (ntile == 1)
+          strip_dot<1>(stg, sm + p.x_off, p.xrow, NG, 0, NG, lane, tot);
+        else
+          strip_dot<2>(stg, sm + p.x_off, p.xrow, NG, 0, NG, lane, tot);
+        const int n0 = (s0 + j) * 16;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        if (nt >= ntile) break;
+        for (int nt = 0; nt < 2; ++nt) {
+          if (nt >= ntile) break;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int id = rid[2 * nt + c];
-          if (id < 0) continue;
-          __nv_bfloat16* yr = p.y + (long long)id * p.N + n0 + g;
-          yr[0] = __float2bfloat16_rn(tot[nt][c] * sx[nt][c]);
-          yr[8] = __float2bfloat16_rn(tot[nt][2 + c] * sx[nt][c]);
+          for (int c = 0; c < 2; ++c) {
+            const int id = rid[2 * nt + c];
+            if (id < 0) continue;
+            __nv_bfloat16* yr = p.y + (long long)id * p.N + n0 + g;
+            yr[0] = __float2bfloat16_rn(tot[nt][c] * sx[nt][c]);
+            yr[8] = __float2bfloat16_rn(tot[nt][2 + c] * sx[nt][c]);
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) b200::mbar_arrive(&empty[slot]);
+    } else {
+      // wps warps per strip: each its share of the groups; partials through shared memory
+      float tot[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if (sj < ns) {
+        const char* stg = ring + slot * p.stage_bytes + sj * rec;
+        const int ga = NG * sp / wps, gb = NG * (sp + 1) / wps;
+        if (ntile == 1)
+          strip_dot<1>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
+        else
+          strip_dot<2>(stg, sm + p.x_off, p.xrow, NG, ga, gb, lane, tot);
+      }
+      __syncwarp();
+      if (lane == 0) b200::mbar_arrive(&empty[slot]);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) part[(wi * 8 + v) * 32 + lane] = tot[v >> 2][v & 3];
+      team_sync(tm, TS);
+      if (sj < ns) {
+        const int n0 = (s0 + sj) * 16;
+        for (int v = sp; v < 4 * ntile; v += wps) {        // value v: tile nt = v / 4, c = v % 4
+          float acc = 0.f;
+          for (int w = 0; w < wps; ++w) acc += part[((sj * wps + w) * 8 + v) * 32 + lane];
+          const int nt = v >> 2, c = v & 3;
+          // (selects, not indexing: the arrays stay in registers)
+          const int id = nt ? ((c & 1) ? rid[3] : rid[2]) : ((c & 1) ? rid[1] : rid[0]);
+          const float f = nt ? ((c & 1) ? sx[1][1] : sx[1][0]) : ((c & 1) ? sx[0][1] : sx[0][0]);
+          if (id >= 0)
+            p.y[(long long)id * p.N + n0 + g + 8 * (c >> 1)] = __float2bfloat16_rn(acc * f);
+        }
+      }
+      team_sync(tm, TS);                     // the partials are read before the next unit's
     }
   }
   if (!ok) atomicExch(&g_moe_err, 1);
@@ -403,7 +442,7 @@ extern "C" {
 int b200_moe_gemm_smem_bytes(int K) {
   if (K <= 0 || K % MOE_GROUP || K > 32768) return -1;
   const MoePlan m = moe_plan(K);
-  return m.nstage < MOE_PAIRS ? -1 : m.smem;
+  return m.nstage < MOE_OCT ? -1 : m.smem;
 }
 
 // r4d_gemm_moe_mxfp4a8_nt_b16 (the closed kernel's ABI, bound with ctypes by the reference's
