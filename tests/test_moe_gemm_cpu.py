@@ -77,3 +77,41 @@ def test_c_entry_argument_codes():
     assert lib.b200_moe_gemm_smem_bytes(2560) > 0 and lib.b200_moe_gemm_smem_bytes(320) > 0
     assert lib.b200_moe_gemm_smem_bytes(1 << 16) == -1 and lib.b200_moe_gemm_smem_bytes(48) == -1
     assert lib.r4d_gemm_moe_mxfp4a8_nt_b16_block() == 16 and lib.r4d_gemm_moe_mxfp4a8_nt_b16_group() == 32
+
+
+def _golden_cases():
+    from conftest import golden
+    z = golden("moe_gemm_reference.npz")
+    n = len([k for k in z.files if k.endswith("_shape")])
+    for i in range(n):
+        yield i, {k[len(f"c{i}_"):]: z[k] for k in z.files if k.startswith(f"c{i}_")}
+
+
+def test_oracle_matches_reference_harness():
+    """The oracle against fixtures made by the reference's own MoE harness
+    (tests/golden/make_moe_golden.py): dequantisation, per-token FP8 quant and the block
+    alignment bit for bit; the fp32 reference output to fp32 rounding (the harness multiplies
+    each expert's rows at once, the oracle each block's)."""
+    for i, c in _golden_cases():
+        E, N, K, M, top_k = (int(v) for v in c["shape"])
+        w, s = torch.from_numpy(c["w"]), torch.from_numpy(c["s"])
+        assert torch.equal(O.dequant_expert(w[0], s[0]), torch.from_numpy(c["deq0"])), i
+        qx, xs = O.quant_fp8_per_token(torch.from_numpy(c["x"]))
+        assert torch.equal(qx.view(torch.uint8), torch.from_numpy(c["qx"])), i
+        assert torch.equal(xs, torch.from_numpy(c["xs"])), i
+        si, ei, npad = O.moe_align_block_size(torch.from_numpy(c["topk"]), 16, E)
+        assert torch.equal(si, torch.from_numpy(c["sorted_ids"])), i
+        assert torch.equal(ei, torch.from_numpy(c["expert_ids"])), i
+        assert torch.equal(npad, torch.from_numpy(c["npad"])), i
+        ref = O.gemm_ref(qx, xs, w, s, si, ei, npad, None, M * top_k, top_k)
+        want = torch.from_numpy(c["out"])
+        assert not torch.isnan(ref).any(), i                  # every routed row is named
+        assert torch.allclose(ref, want, rtol=1e-5, atol=1e-5 * want.abs().max().item()), i
+
+
+def test_pack_of_reference_cases_round_trips():
+    for i, c in _golden_cases():
+        w, s = torch.from_numpy(c["w"]), torch.from_numpy(c["s"])
+        wq, _, wref = MO.pack_mxfp4_moe(w, s)
+        w2, s2 = MO.unpack_mxfp4_moe(wq)
+        assert torch.equal(w2, w) and torch.equal(s2, s) and torch.equal(wref, s.max(dim=2).values), i

@@ -160,3 +160,27 @@ def test_graph_replay(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, want)
+
+
+def test_reference_harness_cases(cuda):
+    """The kernel on the cases tests/golden/make_moe_golden.py made with the reference's own
+    harness functions, against that harness's fp32 output (routed weights applied here, as
+    the harness's down-projection check does)."""
+    from conftest import golden
+    z = golden("moe_gemm_reference.npz")
+    for i in range(len([k for k in z.files if k.endswith("_shape")])):
+        c = {k[len(f"c{i}_"):]: torch.from_numpy(z[k]) for k in z.files if k.startswith(f"c{i}_")}
+        E, N, K, M, top_k = (int(v) for v in c["shape"])
+        mtk = M * top_k
+        wq, ws, wref = MO.pack_mxfp4_moe(c["w"].to(cuda), c["s"].to(cuda))
+        qx = c["qx"].to(cuda).view(torch.float8_e4m3fn)
+        xs, tw = c["xs"].to(cuda), c["tw"].to(cuda)
+        si, ei, npad = c["sorted_ids"].to(cuda), c["expert_ids"].to(cuda), c["npad"].to(cuda)
+        for use_tw in (False, True):
+            y = torch.full((mtk, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+            MO.mxfp4_moe_gemm_into(y, qx, xs, wq, ws, wref, si, ei, npad, tw if use_tw else None, mtk, top_k)
+            torch.cuda.synchronize()
+            want = c["out"].to(cuda) * (tw.unsqueeze(1) if use_tw else 1.0)
+            assert not torch.isnan(y.float()).any(), i
+            rel = ((y.float() - want).abs().max() / want.abs().max()).item()
+            assert rel < TOL, (i, use_tw, rel)
