@@ -4,9 +4,10 @@
 ``gemm_w4a16``), backed by the sm_100a GEMV of csrc/lmhead.cu (``b200_w4_lmhead``; the
 reference's C entry ``r4d_gemm_w4a16_nt_m64`` is exported with the same ABI).
 
-Quantizer: unchanged (draft_w4_lmhead.py:154-198) -- asymmetric per (row, group of 128),
-clip fraction chosen by squared error, the f16 rounding of the scale folded in before the
-codes, integer zero in [-1024, 1024], codes 0..15, dequant ``(q - zero) * scale``.
+Quantizer: the reference's codes (draft_w4_lmhead.py:154-198) -- asymmetric per (row, group
+of 128), clip fraction chosen by squared error, the f16 rounding of the scale folded in before
+the codes, integer zero in [-1024, 1024], codes 0..15, dequant ``(q - zero) * scale`` --
+computed for all clip fractions at once.
 The activation is rounded to f16 exactly as ``x.to(float16)`` (draft_w4_lmhead.py:31-39),
 inside the kernel.
 
@@ -18,8 +19,8 @@ fragments and ``(word >> 4i) & 0x000F000F | 0x64006400`` widens two codes to f16
 ``wsz`` keeps the reference's dword exactly (f16 scale | f16 of -(1024 + zero) << 16,
 [N_pad/16, K/128, 16]).
 
-The launch-config helpers keep the reference's signatures and legality rules so callers and
-env overrides behave the same; the B200 kernel plans its own launch.
+The launch-config helpers keep the reference's signatures, legality rules and choices so
+callers and env overrides behave the same; the B200 kernel plans its own launch.
 """
 from __future__ import annotations
 
@@ -35,10 +36,8 @@ from ._workspace import workspace
 GROUP = 128
 MAX_M = 64
 _WAVE32 = 32
-_KPB = 64
 _MAX_THREADS = 1024
 _MAX_SMEM = 64 * 1024
-_DEQUANT_CHUNK = 8192
 
 _CLIP_GRID = (1.0, 0.95, 0.9, 0.85, 0.8, 0.75, 0.7, 0.65, 0.6)
 
@@ -89,37 +88,36 @@ def quantize_w4(w: torch.Tensor, group: int = 0, clip_grid: tuple[float, ...] | 
                 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """[N, K] -> (q uint8 in 0..15, scale f16 [N, K/group], zero int16 [N, K/group]).
 
-    Asymmetric per (row, group); each clip fraction of the grid is tried and the one with
-    the smallest squared error kept per (row, group); a constant non-zero group is centred
-    on code 8; an all-zero group keeps scale 0, code 0."""
+    The reference's quantizer (draft_w4_lmhead.py:154-198), evaluated for every clip fraction
+    at once: candidate c of a (row, group) spans [mid - c r, mid + c r] around the group's
+    midpoint mid and half-range r; its scale is that span / 15 rounded to f16 (a constant
+    non-zero group instead gets |lo| / 7 and code 8 for its value), its zero the integer
+    nearest to -start / scale within [-1024, 1024], its codes round(w / scale + zero) in 0..15;
+    the candidate with the smallest squared dequantization error wins (the first one on a tie).
+    An all-zero group keeps scale 0, codes 0. Same fp32 operations, so the same codes."""
     group = group or GROUP
     n, k = w.shape
     assert k % group == 0, f"K={k} must be a multiple of the group {group}"
-    wf = w.float().view(n, k // group, group)
-    lo, hi = wf.amin(-1), wf.amax(-1)
-    mid, half = (hi + lo) / 2, (hi - lo) / 2
-    best_err = torch.full_like(lo, float("inf"))
-    best_scale = torch.zeros_like(lo, dtype=torch.float16)
-    best_zero = torch.zeros_like(lo)
-    for c in (clip_grid if clip_grid is not None else _CLIP_GRID):
-        lo_c, hi_c = mid - c * half, mid + c * half
-        scale = ((hi_c - lo_c) / 15.0).clamp(min=0.0).half()
-        flat = (scale.float() == 0) & (lo != 0)
-        scale = torch.where(flat, (lo.abs() / 7.0).half(), scale)
-        sf = scale.float()
-        inv = torch.where(sf > 0, 1.0 / sf.clamp(min=1e-30), torch.zeros_like(sf))
-        zero = torch.where(flat, torch.full_like(lo, 8.0), torch.round(-lo_c * inv)).clamp_(-1024, 1024)
-        q = torch.round(wf * inv.unsqueeze(-1) + zero.unsqueeze(-1)).clamp_(0, 15)
-        err = ((q - zero.unsqueeze(-1)) * sf.unsqueeze(-1) - wf).square().sum(-1)
-        take = err < best_err
-        best_err = torch.where(take, err, best_err)
-        best_scale = torch.where(take, scale, best_scale)
-        best_zero = torch.where(take, zero, best_zero)
-        del scale, sf, inv, zero, q, err
-    sf = best_scale.float()
-    inv = torch.where(sf > 0, 1.0 / sf.clamp(min=1e-30), torch.zeros_like(sf))
-    q = torch.round(wf * inv.unsqueeze(-1) + best_zero.unsqueeze(-1)).clamp_(0, 15)
-    return q.to(torch.uint8).view(n, k), best_scale, best_zero.to(torch.int16)
+    ng = k // group
+    vals = w.float().view(n, ng, 1, group)
+    lo, hi = vals.amin(-1, keepdim=True), vals.amax(-1, keepdim=True)          # [n, ng, 1, 1]
+    fr = torch.tensor(clip_grid if clip_grid is not None else _CLIP_GRID, dtype=torch.float32,
+                      device=w.device).view(1, 1, -1, 1)
+    mid, rad = (hi + lo) / 2, (hi - lo) / 2
+    start = mid - fr * rad                                                     # [n, ng, C, 1]
+    step = ((mid + fr * rad - start) / 15.0).clamp(min=0.0).half()
+    const = (step.float() == 0) & (lo != 0)
+    step = torch.where(const, (lo.abs() / 7.0).half(), step)
+    sf = step.float()
+    rcp = torch.where(sf > 0, 1.0 / sf.clamp(min=1e-30), torch.zeros_like(sf))
+    zero = torch.where(const, torch.full_like(start, 8.0), torch.round(-start * rcp)).clamp_(-1024, 1024)
+    q = torch.round(vals * rcp + zero).clamp_(0, 15)                           # [n, ng, C, group]
+    err = ((q - zero) * sf - vals).square().sum(-1, keepdim=True)              # [n, ng, C, 1]
+    pick = err.argmin(dim=2, keepdim=True)                                     # first minimum
+    q = q.gather(2, pick.expand(n, ng, 1, group))
+    scale = step.gather(2, pick).view(n, ng)
+    zero = zero.gather(2, pick).view(n, ng)
+    return q.to(torch.uint8).view(n, k), scale, zero.to(torch.int16)
 
 
 _NIBBLE = (0, 4, 1, 5, 2, 6, 3, 7)   # nibble of code j: (j & 1) * 4 + (j >> 1)
@@ -144,20 +142,20 @@ def _unpack_codes(wq: torch.Tensor, n_pad: int, k: int, t0: int = 0, t1: int | N
 
 
 def _pack_sz(scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:
-    """(f16 scale, integer zero) [N, K/GROUP] -> int32 [N/16, K/GROUP, 16]
-    (draft_w4_lmhead.py:215-225: -(1024 + zero) is exact in f16 for |zero| <= 1024)."""
+    """(f16 scale, integer zero) [N, K/GROUP] -> int32 [N/16, K/GROUP, 16]: the reference's
+    dword (draft_w4_lmhead.py:215-225), low half the scale's f16 bits, high half the f16 of
+    -(1024 + zero) (exact for |zero| <= 1024), built as two int16 halves viewed as one int32."""
     n, ng = scale.shape
-    sb = scale.contiguous().view(torch.int16).to(torch.int64) & 0xFFFF
-    nz = (-(1024.0 + zero.float())).half().view(torch.int16).to(torch.int64) & 0xFFFF
-    dw = sb | (nz << 16)
-    dw = torch.where(dw >= 2 ** 31, dw - 2 ** 32, dw).to(torch.int32)
-    return dw.view(n // 16, 16, ng).permute(0, 2, 1).contiguous()
+    halves = torch.stack((scale.contiguous().view(torch.int16),
+                          (-(1024.0 + zero.float())).half().view(torch.int16)), dim=-1)
+    return halves.view(torch.int32).view(n // 16, 16, ng).transpose(1, 2).contiguous()
 
 
-def pack_w4a16(weight: torch.Tensor, group: int = 0, chunk_tiles: int = 512,
+def pack_w4a16(weight: torch.Tensor, group: int = 0, chunk_tiles: int = 64,
                clip_grid: tuple[float, ...] | None = None) -> PackedW4:
     """[N, K] bf16/f32 lm_head weight -> PackedW4 in the B200 layout. N is padded to a
-    multiple of 16 with zero rows; chunked over 16-row tiles to bound the transient."""
+    multiple of 16 with zero rows; chunked over 16-row tiles to bound the transient (the
+    quantizer holds every clip candidate: ~36 x the chunk's fp32 bytes)."""
     assert weight.dim() == 2, f"expected [N, K], got {tuple(weight.shape)}"
     _fns()
     group = group or GROUP
@@ -251,29 +249,24 @@ def unpack_w4(packed: PackedW4, dtype: torch.dtype = torch.bfloat16,
 # ---------------------------------------------------------------------------------------
 
 def _legal(k: int, ntiles: int, wv: int, sk: int, npw: int) -> bool:
-    return (wv >= 1 and sk >= 1 and npw in (1, 4)
-            and k % (sk * GROUP) == 0
-            and wv * sk * _WAVE32 <= _MAX_THREADS
-            and wv * npw * sk * 256 * 4 <= _MAX_SMEM
-            and wv * npw <= max(1, ntiles))
-
-
-def _band(m: int) -> int:
-    return 8 if m <= 8 else 16 if m <= 16 else 32 if m <= 32 else 64
-
-
-_CFG_TABLE: dict[int, tuple[tuple[int, int, int, int], ...]] = {
-    8: ((1, 10, 1, 1), (1, 4, 1, 1), (1, 2, 1, 1), (1, 1, 1, 1)),
-    16: ((1, 10, 1, 1), (1, 4, 1, 1), (1, 2, 1, 1), (1, 1, 1, 1)),
-    32: ((1, 4, 4, 1), (1, 2, 4, 1), (1, 1, 4, 1), (1, 4, 1, 1), (1, 1, 1, 1)),
-    64: ((1, 4, 4, 1), (1, 2, 4, 1), (1, 1, 4, 1), (1, 4, 1, 1), (1, 1, 1, 1)),
-}
+    """The reference's resource rules for a (waves, split-K, tiles per wave) launch: K splits
+    into sk whole groups per wave, a block holds at most 1024 threads of 32-wide waves and 64 KB
+    of shared memory (1 KB per wave, tile and split), npw is 1 or 4, and the waves' tiles do not
+    outnumber the N tiles."""
+    threads = wv * sk * _WAVE32
+    smem = wv * npw * sk * 1024
+    return (min(wv, sk) >= 1 and npw in (1, 4) and k % (sk * GROUP) == 0
+            and threads <= _MAX_THREADS and smem <= _MAX_SMEM and wv * npw <= max(1, ntiles))
 
 
 @functools.lru_cache(maxsize=None)
 def pick_cfg(m: int, n_pad: int, k: int) -> tuple[int, int, int, int]:
-    """(WV, SK, NPW, NT) for this M band; env override R4D_W4_LMHEAD_CFG="WV,SK,NPW,NT".
-    Anything illegal falls through to the table / heuristic, exactly as the reference."""
+    """(WV, SK, NPW, NT) as the reference picks it for gfx1201 (draft_w4_lmhead.py:292-344),
+    so that callers and the R4D_W4_LMHEAD_CFG="WV,SK,NPW,NT" override behave the same; the
+    B200 kernel validates the choice and plans its own launch. Rule: one wave, one tile pass;
+    up to 16 rows the deepest split-K of (10, 4, 2, 1) that K allows, above 16 rows four
+    tiles per wave with split-K 4, 2 or 1 (split-K 4 or 1 with one tile per wave once the
+    tiles run short); else a heuristic fill of the block."""
     ntiles = n_pad // 16
     override = os.environ.get("R4D_W4_LMHEAD_CFG")
     if override:
@@ -283,9 +276,13 @@ def pick_cfg(m: int, n_pad: int, k: int) -> tuple[int, int, int, int]:
             wv = sk = npw = nt = 0
         if _legal(k, ntiles, wv, sk, npw) and nt in (0, 1):
             return wv, sk, npw, nt
-    for wv, sk, npw, nt in _CFG_TABLE.get(_band(m), ()):
-        if _legal(k, ntiles, wv, sk, npw):
-            return wv, sk, npw, nt
+    if m <= 16:
+        tries = [(sk, 1) for sk in (10, 4, 2, 1)]
+    else:
+        tries = [(sk, 4) for sk in (4, 2, 1)] + [(4, 1), (1, 1)]
+    for sk, npw in tries:
+        if _legal(k, ntiles, 1, sk, npw):
+            return 1, sk, npw, 1
     sk = next((s for s in (4, 2, 1) if k % (s * GROUP) == 0), 1)
     wv = max(1, min(8, _MAX_THREADS // (sk * _WAVE32), _MAX_SMEM // (sk * 1024), ntiles))
     return wv, sk, 1, 1
