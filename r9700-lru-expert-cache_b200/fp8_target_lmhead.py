@@ -132,6 +132,76 @@ def fp8_lmhead(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, vocab_offset
     return res + (qx, xs) if debug_quant else res
 
 
+class Fp8LmheadStep:
+    """A prepared fp8_lmhead call for a decode loop that reuses its buffers: the activation x,
+    the logits ``out`` (or none), the statistics triple ``stats_out`` and, optionally, the
+    packed float64 [M, 3] triple ``packed_out`` (pack_row_stats' layout, for one device-to-host
+    copy) are checked once, together with the launch stream (the current one at construction)
+    and its workspace; each call then passes only the weight -- which may rotate between
+    same-shaped copies -- to one C call (two with ``packed_out``), with no allocation and no
+    per-tensor checks. With a ``combiner`` (sharded.P2PCombiner) the statistics are the
+    ranks' combined ones, as in P2PCombiner.fp8_head."""
+
+    def __init__(self, x: torch.Tensor, n_rows: int, vocab_offset: int = 0, out: torch.Tensor | None = None,
+                 stats_out: tuple | None = None, packed_out: torch.Tensor | None = None, combiner=None):
+        from ._workspace import workspace
+        _lib.require_cuda("fp8 lm_head step", x, out, packed_out, *(stats_out or ()))
+        if x.dtype != torch.bfloat16 or x.ndim != 2 or not x.is_contiguous():
+            raise ValueError("fp8 lm_head step: x must be a contiguous bf16 [M, K] tensor")
+        M, K = x.shape
+        if K % _BLK:
+            raise ValueError("fp8 lm_head step: K must be a multiple of 128")
+        if out is not None and (out.dtype != torch.bfloat16 or out.shape[0] < M or out.shape[1] < n_rows
+                                or out.stride(1) != 1):
+            raise ValueError("fp8 lm_head step: out must be bf16 [>= M, >= N] with unit column stride")
+        if stats_out is None:
+            stats_out = (torch.empty(M, dtype=torch.float32, device=x.device),
+                         torch.empty(M, dtype=torch.int64, device=x.device),
+                         torch.empty(M, dtype=torch.float32, device=x.device))
+        mx, arg, lse = stats_out
+        if (mx.dtype, arg.dtype, lse.dtype) != (torch.float32, torch.int64, torch.float32) or \
+                min(mx.numel(), arg.numel(), lse.numel()) < M:
+            raise ValueError("fp8 lm_head step: stats_out must be (fp32 [M], int64 [M], fp32 [M])")
+        if packed_out is not None and (packed_out.dtype != torch.float64 or packed_out.numel() < 3 * M
+                                       or not packed_out.is_contiguous()):
+            raise ValueError("fp8 lm_head step: packed_out must be a contiguous float64 [M, 3]")
+        self.x, self.out, self.stats, self.packed = x, out, stats_out, packed_out
+        self._wshape, self._sshape = (n_rows, K), (n_rows // _BLK, K // _BLK)
+        lib = _lib.lmhead()
+        wsp = workspace(x.device)
+        self._wsp = wsp
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        y_ptr = out.data_ptr() if out is not None else 0
+        ldy = out.stride(0) if out is not None else n_rows
+        self._head = (x.data_ptr(), M, K)
+        if combiner is None:
+            self._fn = lib.b200_fp8_lmhead
+            self._tail = (n_rows, int(vocab_offset), y_ptr, ldy, mx.data_ptr(), arg.data_ptr(), lse.data_ptr(),
+                          None, None, wsp.data_ptr(), wsp.numel(), stream)
+        else:
+            self._fn = lib.b200_fp8_lmhead_combined
+            self._tail = (n_rows, int(vocab_offset), y_ptr, ldy, mx.data_ptr(), arg.data_ptr(), lse.data_ptr(),
+                          None, None, wsp.data_ptr(), wsp.numel(), combiner.peers.data_ptr(), combiner.rank,
+                          combiner.world, combiner.counters.data_ptr(), combiner.M_cap, stream)
+        self._pack = None
+        if packed_out is not None:
+            self._pack = (lib.b200_pack_row_stats,
+                          (mx.data_ptr(), arg.data_ptr(), lse.data_ptr(), M, packed_out.data_ptr(), stream))
+
+    def __call__(self, wq: torch.Tensor, ws: torch.Tensor) -> None:
+        if wq.shape != self._wshape or ws.shape != self._sshape:
+            raise ValueError("fp8 lm_head step: the weight's shape differs from the prepared one")
+        rc = self._fn(*self._head, wq.data_ptr(), ws.data_ptr(), *self._tail)
+        if rc != 0:
+            raise RuntimeError(f"b200_fp8_lmhead failed rc={rc}")
+        if self._pack is not None:
+            fn, args = self._pack
+            rc = fn(*args)
+            if rc != 0:
+                raise RuntimeError(f"b200_pack_row_stats failed rc={rc}")
+        _lib.debug_check("b200_fp8_lmhead")
+
+
 def gemm_fp8_block(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor) -> torch.Tensor:
     """bf16 [M, K] @ dequant(W)^T -> bf16 [M, N]; the caller guarantees M <= _MAX_M
     (fp8_target_lmhead.py:70-74). The activation quant runs inside the kernel."""

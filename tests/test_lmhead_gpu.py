@@ -356,3 +356,28 @@ def test_fp8_tc_work_splits(cuda, nblk):
         assert torch.equal(a, b)
     assert P._lib.lmhead().b200_lmhead_error(1) == 0
     del wdq, ref
+
+
+@pytest.mark.parametrize("M", [5, 40])
+def test_fp8_prepared_step_matches_call(cuda, M):
+    """Fp8LmheadStep (buffers checked once, one C call per launch) gives the same logits,
+    statistics and packed triples as fp8_lmhead + pack_row_stats, with rotating weights, and
+    refuses a weight of another shape."""
+    torch.manual_seed(M)
+    w1 = (torch.randn(1280, 2560, device=cuda) * 0.02).bfloat16()
+    w2 = (torch.randn(1280, 2560, device=cuda) * 0.02).bfloat16()
+    packs = [F8.pack_fp8_block(w1), F8.pack_fp8_block(w2)]
+    x = torch.randn(M, 2560, device=cuda, dtype=torch.bfloat16)
+    out = torch.empty(M, 1280, device=cuda, dtype=torch.bfloat16)
+    stats = (torch.empty(M, device=cuda), torch.empty(M, dtype=torch.int64, device=cuda), torch.empty(M, device=cuda))
+    packed = torch.empty(M, 3, dtype=torch.float64, device=cuda)
+    step = F8.Fp8LmheadStep(x, 1280, vocab_offset=384, out=out, stats_out=stats, packed_out=packed)
+    for wq, ws in packs + packs[:1]:
+        step(wq, ws)
+        y, mx, arg, lse = F8.fp8_lmhead(x, wq, ws, vocab_offset=384)
+        torch.cuda.synchronize()
+        assert torch.equal(out, y) and torch.equal(stats[0], mx) and torch.equal(stats[1], arg)
+        assert torch.equal(stats[2], lse)
+        assert torch.equal(packed, P.sharded.pack_row_stats(mx, arg, lse))
+    with pytest.raises(ValueError):
+        step(packs[0][0][:1152], packs[0][1][:9])
