@@ -33,6 +33,7 @@
 //   * guards: table entries >= S and slot_expert entries >= E (undefined in the reference)
 //     are skipped; writes past L / NB are dropped.
 #include <cuda_runtime.h>
+#include <utility>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -112,6 +113,30 @@ __device__ __forceinline__ void block_sum_exscan(int a, int b, int* ra, int* rb,
   *sum_a = sa;
   *pre_b = before + inc - b;
   *tot_b = tb;
+}
+
+// Programmatic dependent launch: each update kernel is launched so that it may start while the
+// kernel ahead of it in the stream is still running; it waits for that kernel (completion and
+// memory visibility) before touching any memory, and lets the next kernel launch at once, so
+// back-to-back updates overlap one launch latency with the previous update's work.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Exp, typename... Act>
+cudaError_t launch_pdl(void (*kern)(Exp...), int threads, int smem, cudaStream_t stream, Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Act>(args)...);
 }
 
 struct ManageArgs {
@@ -362,6 +387,7 @@ __global__ void __launch_bounds__(NT) lru_manage_kernel(ManageArgs a) {
   extern __shared__ __align__(16) char sm[];
   const Smem L = smem_layout(a.E, a.S, TAB_SMEM, false);
   int ids[IDS_REG];
+  pdl_enter();
   manage_core<TAB_SMEM, false>(a, sm, L, ids);
 }
 
@@ -400,6 +426,7 @@ __global__ void __launch_bounds__(NT) lru_fused_kernel(FusedArgs f) {
   const Smem L = smem_layout(E, S, true, true);
   const int tid = threadIdx.x;
   int ids[IDS_REG];
+  pdl_enter();
 
   // ---- the manager (single exit: every output below is always written) ------------------
   // Its last barrier orders the table installs before the reads below; on its early exits
@@ -641,11 +668,9 @@ int r4d_lru_manage(const int* topk_ids, int mk, int E, int S, int max_distinct, 
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
     if (e != cudaSuccess) return (int)e;
   }
-  if (tab)
-    lru_manage_kernel<true><<<1, NT, L.total, stream>>>(a);
-  else
-    lru_manage_kernel<false><<<1, NT, L.total, stream>>>(a);
-  return (int)cudaGetLastError();
+  const cudaError_t e = tab ? launch_pdl(lru_manage_kernel<true>, NT, L.total, stream, a)
+                            : launch_pdl(lru_manage_kernel<false>, NT, L.total, stream, a);
+  return (int)(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // r4d_lru.hip:596-610. L and NB must be exactly what vLLM's moe_align_block_size wrapper
@@ -667,8 +692,8 @@ int r4d_lru_fused(const int* topk_ids, int mk, int E, int S, int max_distinct, i
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Ls.total);
     if (e != cudaSuccess) return (int)e;
   }
-  lru_fused_kernel<<<1, NT, Ls.total, stream>>>(f);
-  return (int)cudaGetLastError();
+  const cudaError_t e = launch_pdl(lru_fused_kernel, NT, Ls.total, stream, f);
+  return (int)(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // r4d_lru.hip:612-629. Sizes are BYTES per expert for each of the six buffers; each must be
