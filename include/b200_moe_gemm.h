@@ -16,6 +16,8 @@
 #ifndef B200_MOE_GEMM_H
 #define B200_MOE_GEMM_H
 
+#include <cuda_runtime.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -39,6 +41,18 @@ void r4d_gemm_moe_mxfp4a8_nt_b16(long qx, long x_scale, long wq, long ws, long w
 int r4d_gemm_moe_mxfp4a8_nt_b16_last_error(void);
 int r4d_gemm_moe_mxfp4a8_nt_b16_block(void);  /* 16 rows per block */
 int r4d_gemm_moe_mxfp4a8_nt_b16_group(void);  /* 32 K-values per E8M0 exponent */
+
+/* The projection's two calls (r4d_mxfp4_moe.py.lru.diff _gemm_split, L584-606) in ONE launch:
+ * the hot call over the resident slots' copies wq_hot with r4d_lru_fused's by-slot blocks
+ * (sorted_hot / eids_hot / npad_hot, capacity em_hot) and the cold call over the full tensors
+ * wq_cold with its by-expert blocks, into the same c. Same result as the two calls; saves the
+ * second launch and balances both calls' units over the SMs together. Returns 0, or the codes
+ * of r4d_gemm_moe_mxfp4a8_nt_b16_last_error (-10 also for a misaligned wq_cold). New. */
+int b200_moe_gemm_hot_cold(const void* qx, const float* x_scale, const void* wq_hot, const void* wq_cold,
+                           void* c, const int* sorted_hot, const int* eids_hot, const int* npad_hot,
+                           int em_hot, const int* sorted_cold, const int* eids_cold, const int* npad_cold,
+                           int em_cold, const float* topk_weights, int mtk, int top_k, int K, int N,
+                           cudaStream_t stream);
 
 /* Dynamic shared memory one launch uses at reduction depth K, or -1 if K is not supported.
  * New (no counterpart in the reference). */

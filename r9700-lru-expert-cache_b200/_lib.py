@@ -64,6 +64,7 @@ LMHEAD_PROTOS = {
     "r4d_gemm_moe_mxfp4a8_nt_b16_last_error": (c_int, []),
     "r4d_gemm_moe_mxfp4a8_nt_b16_block": (c_int, []),
     "r4d_gemm_moe_mxfp4a8_nt_b16_group": (c_int, []),
+    "b200_moe_gemm_hot_cold": (c_int, [c_vp] * 8 + [c_int] + [c_vp] * 3 + [c_int, c_vp] + [c_int] * 4 + [c_vp]),
     "b200_moe_gemm_smem_bytes": (c_int, [c_int]),
     "b200_moe_gemm_error": (c_int, [c_int]),
 }

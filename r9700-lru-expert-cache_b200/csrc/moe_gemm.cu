@@ -51,6 +51,8 @@
 
 #include "common.cuh"
 
+extern "C" int b200_moe_gemm_smem_bytes(int K);
+
 namespace {
 
 constexpr int MOE_BLOCK = 16;             // rows per aligned block (moe_align block size)
@@ -66,16 +68,24 @@ constexpr uint64_t MOE_WAIT_NS = 2000000000ull;
 
 __device__ int g_moe_err = 0;             // 1 = a pipeline wait timed out
 
-struct MoeParams {
-  const uint8_t* qx;       // e4m3 [tokens, K]; row i of the GEMM reads token i / top_k
-  const float* xs;         // fp32 [tokens]
+// One expert set's call: its weights and its aligned blocks. A launch takes one set (the
+// reference's per-call entry) or two (the hot and the cold call of a projection at once).
+struct MoeSet {
   const uint8_t* wq;
-  __nv_bfloat16* y;        // [mtk, N]
   const int* sorted;       // [em]
   const int* eids;         // [em / 16]
   const int* npad;         // [1]
+  int em;
+};
+
+struct MoeParams {
+  const uint8_t* qx;       // e4m3 [tokens, K]; row i of the GEMM reads token i / top_k
+  const float* xs;         // fp32 [tokens]
+  __nv_bfloat16* y;        // [mtk, N]
   const float* tw;         // [mtk] or nullptr
-  int em, mtk, top_k, K, N;
+  MoeSet set[2];
+  int nsets;
+  int mtk, top_k, K, N;
   int nstage, stage_bytes, xrow, x_off, ring_off, run;   // run = R strips per unit
   int xch_off;                                            // the teams' exchange buffers
 };
@@ -121,9 +131,16 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
 // (wps = 2), and a team holds R such pairs, at least one; with R >= 8 every warp takes whole
 // strips (wps = 1) in teams of 8 (16 for R >= 16). TS warps per team, NT = 16 / TS teams (a
 // divisor of the ring's stage count, which is a multiple of 8).
-__host__ __device__ __forceinline__ void team_plan(int run, int& TS, int& NT, int& wps) {
-  wps = run < MOE_OCT ? 2 : 1;
-  TS = run < MOE_OCT ? 2 * run : (run >= 2 * MOE_OCT ? MOE_NC : MOE_OCT);
+// With few units per CTA (decode at a token or two: up to 4), the split runs 8 ways (teams of
+// 8, wps = 8 / R) so that a unit's groups spread over more warps.
+__host__ __device__ __forceinline__ void team_plan(int run, int upc, int& TS, int& NT, int& wps) {
+  if (run < MOE_OCT && upc <= 4) {
+    wps = MOE_OCT / run;
+    TS = MOE_OCT;
+  } else {
+    wps = run < MOE_OCT ? 2 : 1;
+    TS = run < MOE_OCT ? 2 * run : (run >= 2 * MOE_OCT ? MOE_NC : MOE_OCT);
+  }
   NT = MOE_NC / TS;
 }
 
@@ -192,9 +209,21 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
   const int NS = p.N / 16, NG = p.K / MOE_GROUP, rec = NG * 272;
   const int NR = (NS + p.run - 1) / p.run;           // runs (units) per block
 
+  // the units of the live blocks of both sets (set 0's blocks first), split evenly over the
+  // CTAs; global block gb < live0 is set 0's block gb, else set 1's block gb - live0
+  const int live0 = min(max(p.set[0].npad[0], 0), p.set[0].em) / MOE_BLOCK;
+  const int live1 = p.nsets > 1 ? min(max(p.set[1].npad[0], 0), p.set[1].em) / MOE_BLOCK : 0;
+  const long long units = (long long)(live0 + live1) * NR;
+  const int u0 = (int)(units * blockIdx.x / gridDim.x), u1 = (int)(units * (blockIdx.x + 1) / gridDim.x);
+  const int upc = (int)((units + gridDim.x - 1) / gridDim.x);
+  auto block_set = [&](int gb, int& lb) -> const MoeSet& {
+    lb = gb < live0 ? gb : gb - live0;
+    return p.set[gb < live0 ? 0 : 1];
+  };
+
   if (threadIdx.x == 0) {
     int ts, nt, wps0;
-    team_plan(p.run, ts, nt, wps0);
+    team_plan(p.run, upc, ts, nt, wps0);
     for (int i = 0; i < p.nstage; ++i) {
       b200::mbar_init(&full[i], 1);
       b200::mbar_init(&empty[i], ts);       // every warp of the unit's team
@@ -206,23 +235,20 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
   __syncthreads();
   const uint64_t deadline = b200::globaltimer_ns() + MOE_WAIT_NS;
 
-  // the units of the live blocks, split evenly over the CTAs
-  const int live = min(max(p.npad[0], 0), p.em) / MOE_BLOCK;
-  const long long units = (long long)live * NR;
-  const int u0 = (int)(units * blockIdx.x / gridDim.x), u1 = (int)(units * (blockIdx.x + 1) / gridDim.x);
-
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = b200::l2_policy_evict_first();
       bool ok = true;
       int q = 0, nb = 0, pend = -1, b = u0 / NR, s = u0 - b * NR, e = -1, cur_b = -1;
+      const uint8_t* wsrc = nullptr;          // the current block's set's weights
       // block blk's row ids and activation rows into the buffer (its previous user released it)
       auto load_x = [&](int blk) {
-        int ids[MOE_BLOCK], nlive = 0;
+        int ids[MOE_BLOCK], nlive = 0, lb;
+        const MoeSet& bs = block_set(blk, lb);
 #pragma unroll
         for (int r = 0; r < MOE_BLOCK; ++r) {
-          const int id = p.sorted[blk * MOE_BLOCK + r];
+          const int id = bs.sorted[lb * MOE_BLOCK + r];
           ids[r] = (id >= 0 && id < p.mtk) ? id : -1;
           rowid[r] = ids[r];
           nlive += ids[r] >= 0;
@@ -251,7 +277,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
         }
         if (b != cur_b) {
           cur_b = b;
-          e = p.eids[b];
+          int lb;
+          const MoeSet& bs = block_set(b, lb);
+          e = bs.eids[lb];
+          wsrc = bs.wq;
           if (e < 0) continue;
           if (pend >= 0) {                  // every unit before it is issued: this wait ends
             if (!b200::mbar_wait_bounded(xempty, (nb - 1) & 1, deadline)) {
@@ -287,7 +316,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
         const int s0 = s * p.run, ns = min(p.run, NS - s0);
         const uint32_t bytes = (uint32_t)(ns * rec);
         b200::mbar_arrive_expect_tx(&full[slot], bytes);
-        b200::bulk_g2s_stream(dst, p.wq + ((long long)e * NS + s0) * rec, bytes, &full[slot], pol);
+        b200::bulk_g2s_stream(dst, wsrc + ((long long)e * NS + s0) * rec, bytes, &full[slot], pol);
         ++q;
       }
       if (ok && pend >= 0) {
@@ -313,7 +342,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
   // the values. (Few large strips per unit: small teams, so that more units are in flight; many
   // small strips: a strip per warp and no reduction.)
   int TS, NT, wps;
-  team_plan(p.run, TS, NT, wps);
+  team_plan(p.run, upc, TS, NT, wps);
   const int cw = warp - 1, tm = cw / TS, wi = cw - tm * TS, g = lane >> 2, t = lane & 3;
   float* part = reinterpret_cast<float*>(sm + p.xch_off) + tm * TS * 256;   // [TS warps][8 values][32]
   const int sj = wi / wps, sp = wi - sj * wps;             // this warp's strip in the unit, its part
@@ -328,7 +357,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_mxfp4_kernel(MoeParams p) 
     }
     if (b != cur_b) {
       cur_b = b;
-      e = p.eids[b];
+      int lb;
+      e = block_set(b, lb).eids[lb];
       if (e < 0) continue;
       if (nb > 0) {                          // done with the previous block's activation
         __syncwarp();
@@ -432,6 +462,51 @@ int moe_num_sms() {
 
 int g_moe_last_rc = 0;
 
+// Checks, plan and launch for one or two expert sets; 0, -1 em < 16 / mtk < 0 / top_k < 1,
+// -2 N % 16, -3 K % 32 or K too deep for shared memory, -10 misaligned qx / weights, else a
+// CUDA error.
+int moe_launch(const void* qx, const float* x_scale, void* c, const float* tw, const MoeSet* sets, int nsets,
+               int mtk, int top_k, int K, int N, cudaStream_t stream) {
+  for (int i = 0; i < nsets; ++i)
+    if (sets[i].em < MOE_BLOCK) return -1;
+  if (mtk < 0 || top_k < 1) return -1;
+  if (N <= 0 || N % 16) return -2;
+  const int smem = b200_moe_gemm_smem_bytes(K);
+  if (smem < 0) return -3;
+  if ((reinterpret_cast<uintptr_t>(qx) & 15) || (reinterpret_cast<uintptr_t>(sets[0].wq) & 15)) return -10;
+  if (mtk == 0) return 0;
+  MoeParams p{};
+  p.qx = static_cast<const uint8_t*>(qx);
+  p.xs = x_scale;
+  p.y = static_cast<__nv_bfloat16*>(c);
+  p.tw = tw;
+  for (int i = 0; i < nsets; ++i) p.set[i] = sets[i];
+  p.nsets = nsets;
+  p.mtk = mtk;
+  p.top_k = top_k;
+  p.K = K;
+  p.N = N;
+  const MoePlan m = moe_plan(K);
+  p.xrow = m.xrow;
+  p.x_off = m.x_off;
+  p.ring_off = m.ring_off;
+  p.run = m.run;
+  p.stage_bytes = m.stage_bytes;
+  p.nstage = m.nstage;
+  p.xch_off = m.ring_off + m.nstage * m.stage_bytes;
+  static bool smem_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !smem_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               MOE_SMEM_CAP);
+    if (e != cudaSuccess) return (int)e;
+    smem_set[dev] = true;
+  }
+  moe_mxfp4_kernel<<<moe_num_sms(), MOE_THREADS, smem, stream>>>(p);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace
 
 extern "C" {
@@ -460,45 +535,22 @@ void r4d_gemm_moe_mxfp4a8_nt_b16(long qx, long x_scale, long wq, long ws, long w
                                  long expert_ids, long num_post_pad, long topk_weights, int em, int mtk,
                                  int top_k, int K, int N, int wv, int sk, int npw, long stream) {
   (void)ws; (void)wref; (void)wv; (void)sk; (void)npw;
-  if (em < MOE_BLOCK || mtk < 0 || top_k < 1) { g_moe_last_rc = -1; return; }
-  if (N <= 0 || N % 16) { g_moe_last_rc = -2; return; }
-  const int smem = b200_moe_gemm_smem_bytes(K);
-  if (smem < 0) { g_moe_last_rc = -3; return; }
-  if ((qx & 15) || (wq & 15)) { g_moe_last_rc = -10; return; }
-  if (mtk == 0) { g_moe_last_rc = 0; return; }
-  MoeParams p{};
-  p.qx = reinterpret_cast<const uint8_t*>(qx);
-  p.xs = reinterpret_cast<const float*>(x_scale);
-  p.wq = reinterpret_cast<const uint8_t*>(wq);
-  p.y = reinterpret_cast<__nv_bfloat16*>(c);
-  p.sorted = reinterpret_cast<const int*>(sorted_ids);
-  p.eids = reinterpret_cast<const int*>(expert_ids);
-  p.npad = reinterpret_cast<const int*>(num_post_pad);
-  p.tw = reinterpret_cast<const float*>(topk_weights);
-  p.em = em;
-  p.mtk = mtk;
-  p.top_k = top_k;
-  p.K = K;
-  p.N = N;
-  const MoePlan m = moe_plan(K);
-  p.xrow = m.xrow;
-  p.x_off = m.x_off;
-  p.ring_off = m.ring_off;
-  p.run = m.run;
-  p.stage_bytes = m.stage_bytes;
-  p.nstage = m.nstage;
-  p.xch_off = m.ring_off + m.nstage * m.stage_bytes;
-  static bool smem_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !smem_set[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(moe_mxfp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               MOE_SMEM_CAP);
-    if (e != cudaSuccess) { g_moe_last_rc = (int)e; return; }
-    smem_set[dev] = true;
-  }
-  moe_mxfp4_kernel<<<moe_num_sms(), MOE_THREADS, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
-  g_moe_last_rc = (int)cudaGetLastError();
+  MoeSet one{reinterpret_cast<const uint8_t*>(wq), reinterpret_cast<const int*>(sorted_ids),
+             reinterpret_cast<const int*>(expert_ids), reinterpret_cast<const int*>(num_post_pad), em};
+  g_moe_last_rc = moe_launch(reinterpret_cast<const void*>(qx), reinterpret_cast<const float*>(x_scale),
+                             reinterpret_cast<void*>(c), reinterpret_cast<const float*>(topk_weights), &one, 1,
+                             mtk, top_k, K, N, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// The projection's hot and cold calls in one launch (see include/b200_moe_gemm.h).
+int b200_moe_gemm_hot_cold(const void* qx, const float* x_scale, const void* wq_hot, const void* wq_cold, void* c,
+                           const int* sorted_hot, const int* eids_hot, const int* npad_hot, int em_hot,
+                           const int* sorted_cold, const int* eids_cold, const int* npad_cold, int em_cold,
+                           const float* topk_weights, int mtk, int top_k, int K, int N, cudaStream_t stream) {
+  if ((reinterpret_cast<uintptr_t>(wq_cold) & 15)) return -10;
+  MoeSet two[2] = {{static_cast<const uint8_t*>(wq_hot), sorted_hot, eids_hot, npad_hot, em_hot},
+                   {static_cast<const uint8_t*>(wq_cold), sorted_cold, eids_cold, npad_cold, em_cold}};
+  return moe_launch(qx, x_scale, c, topk_weights, two, 2, mtk, top_k, K, N, stream);
 }
 
 int r4d_gemm_moe_mxfp4a8_nt_b16_last_error(void) { return g_moe_last_rc; }

@@ -123,24 +123,12 @@ def _check_cfg(em: int, N: int, K: int, wv: int, sk: int, npw: int) -> None:
         raise ValueError(f"r4d_mxfp4_moe_gemm: invalid shape/config em={em} N={N} K={K} cfg={(wv, sk, npw)}")
 
 
-def mxfp4_moe_gemm_into(y: torch.Tensor, qx: torch.Tensor, x_scale: torch.Tensor, wq: torch.Tensor,
-                        ws: torch.Tensor, wref: torch.Tensor, sorted_ids: torch.Tensor,
-                        expert_ids: torch.Tensor, num_post_pad: torch.Tensor,
-                        topk_weights: torch.Tensor | None, mtk: int, top_k: int,
-                        wv: int = 1, sk: int = 1, npw: int = 1) -> None:
-    """y[i, :] for every row i the aligned blocks name (the rows of a block share its expert):
-    bf16(topk_weights[i] * x_scale[i // top_k] * qx[i // top_k] . W_e); other rows untouched.
-    qx e4m3 [tokens, K], x_scale fp32 [tokens] (or [tokens, 1]); wq from pack_mxfp4_moe (or the
-    hot experts' compact copies indexed by slot); ws / wref are the reference's remaining
-    arguments (any CUDA tensors: the kernel reads codes and exponents from wq); y bf16
-    [mtk, N]."""
-    _lib.require_cuda("r4d_mxfp4_moe_gemm", y, qx, x_scale, wq, ws, wref, sorted_ids, expert_ids,
-                      num_post_pad, topk_weights)
+def _moe_check(y, qx, x_scale, wq, sorted_ids, expert_ids, num_post_pad, topk_weights, mtk):
+    """The op's argument checks; returns (K, N, em, x_scale flat, topk_weights flat or None)."""
     K = qx.shape[1]
     E, NS, R = wq.shape
     G = R // 272
     N = NS * 16
-    em = sorted_ids.numel()
     if y.shape != (mtk, N) or y.dtype != torch.bfloat16 or not y.is_contiguous():
         raise ValueError(f"r4d_mxfp4_moe_gemm: y must be contiguous bf16 [{mtk}, {N}]")
     if G * MOE_GROUP != K or qx.dtype != torch.float8_e4m3fn or not qx.is_contiguous():
@@ -158,6 +146,23 @@ def mxfp4_moe_gemm_into(y: torch.Tensor, qx: torch.Tensor, x_scale: torch.Tensor
         tw = topk_weights.reshape(-1)
         if tw.dtype != torch.float32 or tw.numel() < mtk or not tw.is_contiguous():
             raise ValueError("r4d_mxfp4_moe_gemm: topk_weights must be contiguous fp32 [mtk]")
+    return K, N, sorted_ids.numel(), xs, tw
+
+
+def mxfp4_moe_gemm_into(y: torch.Tensor, qx: torch.Tensor, x_scale: torch.Tensor, wq: torch.Tensor,
+                        ws: torch.Tensor, wref: torch.Tensor, sorted_ids: torch.Tensor,
+                        expert_ids: torch.Tensor, num_post_pad: torch.Tensor,
+                        topk_weights: torch.Tensor | None, mtk: int, top_k: int,
+                        wv: int = 1, sk: int = 1, npw: int = 1) -> None:
+    """y[i, :] for every row i the aligned blocks name (the rows of a block share its expert):
+    bf16(topk_weights[i] * x_scale[i // top_k] * qx[i // top_k] . W_e); other rows untouched.
+    qx e4m3 [tokens, K], x_scale fp32 [tokens] (or [tokens, 1]); wq from pack_mxfp4_moe (or the
+    hot experts' compact copies indexed by slot); ws / wref are the reference's remaining
+    arguments (any CUDA tensors: the kernel reads codes and exponents from wq); y bf16
+    [mtk, N]."""
+    _lib.require_cuda("r4d_mxfp4_moe_gemm", y, qx, x_scale, wq, ws, wref, sorted_ids, expert_ids,
+                      num_post_pad, topk_weights)
+    K, N, em, xs, tw = _moe_check(y, qx, x_scale, wq, sorted_ids, expert_ids, num_post_pad, topk_weights, mtk)
     _check_cfg(em, N, K, wv, sk, npw)
     lib = _lib.lmhead()
     lib.r4d_gemm_moe_mxfp4a8_nt_b16(qx.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
@@ -183,12 +188,24 @@ def gemm_split(y: torch.Tensor, qx: torch.Tensor, xs: torch.Tensor, full: tuple,
                align_hot: tuple, align_cold: tuple, tw: torch.Tensor | None, mtk: int, top_k: int,
                skip_cold: bool = False, cfg: tuple = (1, 1, 1)) -> None:
     """_gemm_split (r4d_mxfp4_moe.py.lru.diff L584-606): the hot call over the resident slots'
-    copies (`hot` = (wq, ws, wref) indexed by slot, align_hot from r4d_lru_fused), then the cold
-    call over the full tensors (`full`, indexed by expert id, align_cold); the two fill disjoint
-    rows of y. skip_cold drops the cold call when the caller knows it is empty."""
-    mxfp4_moe_gemm_into(y, qx, xs, *hot, *align_hot, tw, mtk, top_k, *cfg)
-    if not skip_cold:
-        mxfp4_moe_gemm_into(y, qx, xs, *full, *align_cold, tw, mtk, top_k, *cfg)
+    copies (`hot` = (wq, ws, wref) indexed by slot, align_hot from r4d_lru_fused) and the cold
+    call over the full tensors (`full`, indexed by expert id, align_cold), filling disjoint rows
+    of y -- here in ONE launch (b200_moe_gemm_hot_cold), which is the two calls' result without
+    the second launch. skip_cold runs the hot call alone."""
+    if skip_cold:
+        mxfp4_moe_gemm_into(y, qx, xs, *hot, *align_hot, tw, mtk, top_k, *cfg)
+        return
+    _lib.require_cuda("r4d_mxfp4_moe_gemm", y, qx, xs, hot[0], full[0], *align_hot, *align_cold, tw)
+    K, N, em_h, xsf, twf = _moe_check(y, qx, xs, hot[0], *align_hot, tw, mtk)
+    K2, N2, em_c, _, _ = _moe_check(y, qx, xs, full[0], *align_cold, tw, mtk)
+    _check_cfg(em_h, N, K, *cfg)
+    _check_cfg(em_c, N, K, *cfg)
+    rc = _lib.lmhead().b200_moe_gemm_hot_cold(
+        qx.data_ptr(), xsf.data_ptr(), hot[0].data_ptr(), full[0].data_ptr(), y.data_ptr(),
+        align_hot[0].data_ptr(), align_hot[1].data_ptr(), align_hot[2].data_ptr(), em_h,
+        align_cold[0].data_ptr(), align_cold[1].data_ptr(), align_cold[2].data_ptr(), em_c,
+        0 if twf is None else twf.data_ptr(), mtk, top_k, K, N, torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "b200_moe_gemm_hot_cold")
 
 
 def _register_moe_ops() -> None:
