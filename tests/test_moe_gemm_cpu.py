@@ -115,3 +115,19 @@ def test_pack_of_reference_cases_round_trips():
         wq, _, wref = MO.pack_mxfp4_moe(w, s)
         w2, s2 = MO.unpack_mxfp4_moe(wq)
         assert torch.equal(w2, w) and torch.equal(s2, s) and torch.equal(wref, s.max(dim=2).values), i
+
+
+def test_hot_cold_entry_argument_codes():
+    """b200_moe_gemm_hot_cold refuses bad arguments before any CUDA call (no GPU here)."""
+    lib = P._lib.lmhead()
+    f = lib.b200_moe_gemm_hot_cold
+    A = 16 * 1024
+    def call(wq_cold=A, em_hot=800, em_cold=800, N=640, K=2560, mtk=40, top_k=10, qx=A):
+        return f(qx, A, A, wq_cold, A, A, A, A, em_hot, A, A, A, em_cold, None, mtk, top_k, K, N, None)
+    assert call(wq_cold=A + 8) == -10
+    assert call(qx=A + 4) == -10
+    assert call(em_hot=8) == -1 and call(em_cold=8) == -1
+    assert call(top_k=0) == -1 and call(mtk=-1) == -1
+    assert call(N=650) == -2
+    assert call(K=2560 + 16) == -3
+    assert call(mtk=0) == 0                      # nothing to do: returns before any launch

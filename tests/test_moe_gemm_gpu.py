@@ -184,3 +184,55 @@ def test_reference_harness_cases(cuda):
             assert not torch.isnan(y.float()).any(), i
             rel = ((y.float() - want).abs().max() / want.abs().max()).item()
             assert rel < TOL, (i, use_tw, rel)
+
+
+@pytest.mark.parametrize("E,N,K,M,top_k", [
+    (16, 96, 1280, 6, 4),      # two strips per unit: teams of four (or of eight at few units)
+    (8, 16, 64, 20, 2),        # one strip, 32 strips per unit (whole-strip warps, team of 16)
+    (12, 48, 160, 3, 3),       # ragged run: 3 strips in a 16-strip unit
+    (64, 640, 2560, 40, 10),   # many units per CTA: K split in pairs
+    (64, 640, 2560, 1, 2),     # at most four units per CTA: K split eight ways
+])
+def test_team_plans(cuda, E, N, K, M, top_k):
+    """Every consumer team plan against the oracle (the split of a strip's K between warps and
+    the reduction of their partial sums), with routed weights."""
+    y, ref = _run(cuda, E, N, K, M, top_k, True, E * 1000 + K + M)
+    _check(y, ref, f"{E}x{N}x{K} M={M} k={top_k}")
+
+
+def test_hot_cold_entry_edges(cuda):
+    """b200_moe_gemm_hot_cold with an empty hot list, an empty cold list and both empty, and
+    with expert id -1 in either list: the rows of the live blocks, nothing else."""
+    E, N, K, M, top_k = 32, 64, 256, 6, 3
+    w, s, x, topk, tw = O.build_case(E, N, K, M, top_k, 41, cuda)
+    qx, xs = O.quant_fp8_per_token(x)
+    mtk = M * top_k
+    wq, ws, wref = MO.pack_mxfp4_moe(w, s)
+    si, ei, npad = O.moe_align_block_size(topk, 16, E)
+    ref = O.gemm_ref(qx, xs, w, s, si, ei, npad, tw, mtk, top_k)
+    empty = (torch.full_like(si, mtk), torch.full_like(ei, -1), torch.zeros_like(npad))
+    full = (wq, ws, wref)
+    for hot_a, cold_a, want in (((si, ei, npad), empty, ref), (empty, (si, ei, npad), ref),
+                                (empty, empty, torch.full_like(ref, float("nan")))):
+        y = torch.full((mtk, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+        MO.gemm_split(y, qx, xs, full, full, hot_a, cold_a, tw, mtk, top_k)
+        torch.cuda.synchronize()
+        _check(y, want, "edge")
+    # expert -1 on the first block of the hot list and on the last live block of the cold list
+    nb = int(npad.item()) // 16
+    half = nb // 2
+    h_si, c_si = si.clone(), si.clone()
+    h_ei, c_ei = ei.clone(), ei.clone()
+    h_ei[half:] = -1
+    c_ei[:half] = -1
+    h_ei[0] = -1
+    c_ei[nb - 1] = -1
+    y = torch.full((mtk, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+    MO.gemm_split(y, qx, xs, full, full, (h_si, h_ei, npad), (c_si, c_ei, npad), tw, mtk, top_k)
+    torch.cuda.synchronize()
+    want = ref.clone()
+    dead = torch.cat([si[0:16], si[(nb - 1) * 16: nb * 16]])
+    dead = dead[dead < mtk].long()
+    want[dead] = float("nan")
+    _check(y, want, "expert -1")
+    assert P._lib.lmhead().b200_moe_gemm_error(1) == 0
