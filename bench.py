@@ -320,6 +320,74 @@ def lru_bench(P, rank: int, world: int, dev, reps: int = 20) -> dict:
             "method": "52 fused launches in one CUDA graph, median over replays"}
 
 
+def lru_forced_routes(rng, hot: list, E: int, k: int, tokens: int = 20) -> np.ndarray:
+    """tokens x top-10 ids, 10 distinct per token, naming exactly k distinct experts that are not
+    resident (spread over the tokens in order) and otherwise resident ones drawn from a pool of
+    100 - k, so that at most 100 distinct experts are routed (below max_distinct = 128: the
+    update is never a read-through)."""
+    cold = np.setdiff1d(np.arange(E), np.asarray(hot))
+    miss = rng.choice(cold, k, replace=False)
+    pool = rng.choice(np.asarray(hot), 100 - k, replace=False)
+    rows, mi = [], 0
+    for _ in range(tokens):
+        nm = min(TOPK, k - mi)
+        ids = list(miss[mi:mi + nm]) + list(rng.choice(pool, TOPK - nm, replace=False))
+        mi += nm
+        rows.append(ids)
+    return np.asarray(rows, dtype=np.int32)
+
+
+def lru_inserts_sweep(P, dev, ks=(0, 1, 2, 4, 8, 13, 14, 32, 64), reps: int = 6) -> dict:
+    """us per layer with exactly k inserts per layer (the reference's forced-k states,
+    README.md:97-100: S = 257 warm slots, max_inserts 64): 52 layers' updates in one CUDA
+    graph, each layer's cache state restored before every replay (outside the timed region),
+    for the manager alone (r4d_lru_manage) and the fused update (r4d_lru_fused)."""
+    rng = np.random.default_rng(2024)
+    res = {}
+    for k in ks:
+        layers, ids = [], []
+        for _ in range(LAYERS):
+            hot = sorted(rng.choice(E_EXPERTS, S_SLOTS, replace=False).tolist())
+            layers.append(P.lru.LruLayer.warm(hot, E_EXPERTS, dev, stamps=torch.as_tensor(rng.permutation(S_SLOTS) + 1),
+                                              step=S_SLOTS, max_inserts=64))
+            ids.append(torch.as_tensor(lru_forced_routes(rng, hot, E_EXPERTS, k).ravel(), device=dev))
+        snaps = [lay.snapshot() for lay in layers]
+        outs = [lay.new_align_outputs(ids[0].numel()) for lay in layers]
+        row = {}
+        for kind in ("manage", "fused"):
+            def step():
+                for lay, i, o in zip(layers, ids, outs):
+                    if kind == "manage":
+                        lay.manage(i)
+                    else:
+                        lay.fused(i, o)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                step()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            times = []
+            for r in range(reps):
+                for lay, sn in zip(layers, snaps):
+                    lay.restore(sn)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                g.replay()
+                b.record()
+                torch.cuda.synchronize(dev)
+                times.append(a.elapsed_time(b) * 1e3 / LAYERS)
+            n_ins = statistics.mean(int(l.n_miss.item()) for l in layers)
+            assert n_ins == k, (kind, k, n_ins)
+            del g
+            row[kind] = statistics.median(times[1:])
+        res[f"k{k}"] = row
+    return res
+
+
 def lru_gather_bench(P, dev, experts: int = 128) -> dict:
     """lru_gather from pinned host memory (UVA) into device slots: the six per-expert slabs of
     the reference's MXFP4 MoE layer (819200 + 409600 + 51200 + 640 + 25600 + 2560 B = 1.31 MB per
@@ -1075,6 +1143,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_extras:
         ops = ops_bench(P, dev)
         ops["lru_gather_pinned_host"] = lru_gather_bench(P, dev)
+        ops["lru_us_per_layer_by_inserts"] = lru_inserts_sweep(P, dev)
         ceiling = probe_ceiling(P, dev, n_loc * K_HID)
     if world > 1:
         dist.barrier()
