@@ -116,6 +116,23 @@ B200_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t dead
   return true;
 }
 
+// Stage tags of a ring whose slots several consumer warps share: the producer stores (release)
+// the index of the stage it is about to issue into a slot; a consumer that sees its stage's
+// index there (acquire) knows the slot's previous round has been consumed, so its parity wait
+// on the slot's barrier can only end on this stage's own phase.
+B200_DEVINL void tag_publish(int* tag, int q) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(tag)), "r"(q) : "memory");
+}
+
+B200_DEVINL bool tag_wait_bounded(const int* tag, int q, uint64_t deadline_ns) {
+  for (uint32_t n = 0;; ++n) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(tag)) : "memory");
+    if (v == q) return true;
+    if ((n & 63u) == 63u && globaltimer_ns() > deadline_ns) return false;
+  }
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (transaction bytes).
 // Both addresses 16-byte aligned and `bytes` a multiple of 16.
 B200_DEVINL void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

@@ -92,6 +92,7 @@ struct Params {
   int pdl;           // 1: launched as the programmatic dependent of the activation kernel
   int kw;            // tcgen05 path: 128-K blocks per stage
   int cs_off;        // tcgen05 path: per-accumulator scale vectors in shared memory
+  int tagged;        // GEMV: consumers check stage tags (the ring's slots are not owned)
   float* px;         // tcgen05 path: partial accumulators of blocks split along K
   int* flags;        // tcgen05 path: split pairs' tickets and ready flags
   // vocabulary-sharded combine fused into the statistics merge (peers == nullptr: none)
@@ -369,8 +370,10 @@ __device__ __forceinline__ void stats_write_partial(const Params& p, const b200:
 // ---- the kernel ------------------------------------------------------------------------------
 
 // Shared-memory header of the GEMV: full/empty barriers [0, 256), the activation barrier at
-// 256, per-warp row statistics from 384, the "last CTA" flag after them.
+// 256, the stage tags of the ring slots from 320, per-warp row statistics from 384, the "last
+// CTA" flag after them.
 constexpr int GEMV_XBAR = 256;
+constexpr int GEMV_TAGS = 320;
 constexpr int GEMV_HDR_RED = 384;
 __host__ __device__ constexpr int gemv_hdr(int nc) { return GEMV_HDR_RED + nc * MAXM * 12 + 16; }
 
@@ -391,6 +394,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   uint64_t* full = reinterpret_cast<uint64_t*>(sm);
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* x_bar = reinterpret_cast<uint64_t*>(sm + GEMV_XBAR);
+  int* tag = reinterpret_cast<int*>(sm + GEMV_TAGS);
   b200::RowStat* red = reinterpret_cast<b200::RowStat*>(sm + GEMV_HDR_RED);   // [NC][MAXM]
   char* ring = sm + p.ring_off;
 
@@ -398,6 +402,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
     for (int i = 0; i < p.nstage; ++i) {
       b200::mbar_init(&full[i], 1);
       b200::mbar_init(&empty[i], 1);
+      tag[i] = -1;
     }
     b200::mbar_init(x_bar, 1);
     b200::fence_mbar_init();
@@ -425,6 +430,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
           ok = false;
           break;
         }
+        if (p.tagged) b200::tag_publish(&tag[slot], q);
         const int strip = s0 + q / CH, ch = q % CH;
         const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
         const long long blk = (long long)strip * KB + kb0;
@@ -461,7 +467,10 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
       for (int nt = 0; nt < NT8; ++nt) tot[nt][0] = tot[nt][1] = tot[nt][2] = tot[nt][3] = 0.f;
       for (int ch = 0; ch < CH; ++ch) {
         const int q = ls * CH + ch, slot = q % p.nstage;
-        const bool got = b200::mbar_wait_bounded(&full[slot], (q / p.nstage) & 1, deadline);
+        // (tagged ring) the stage is in its slot, so the parity wait cannot end on the slot's
+        // previous round, whose copy may still be landing; then it has landed
+        const bool got = (!p.tagged || b200::tag_wait_bounded(&tag[slot], q, deadline)) &&
+                         b200::mbar_wait_bounded(&full[slot], (q / p.nstage) & 1, deadline);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -1547,11 +1556,14 @@ int allow_full_smem(const void* kern, bool (&done)[HOST_MAX_DEVICES]) {
 }
 
 // Fill in the GEMV's shared-memory plan; returns the dynamic smem bytes, or -1 if it cannot fit.
-// Consumer warp c takes strips c, c + NC, ... of CH = ceil(KB / kps) stages each, and waits on
-// a stage slot by the parity of its round; the wait is unambiguous only while the slot's
-// previous round has already been issued, which holds when nstage >= (NC - 1) * CH + 1 (the
-// producer issues in order, and a consumer starting a strip has finished a stage at most
-// (NC - 1) * CH + 1 positions earlier). Plans below that bound are rejected.
+// Consumer warp c takes strips c, c + NC, ... of CH = ceil(KB / kps) stages each and waits on
+// a slot by the parity of the stage's round. That wait must not end on the slot's previous
+// round, whose copy may still be landing (issued is not enough: two bulk copies may complete
+// out of order). When nstage is a multiple of NC * CH every slot is owned by one consumer,
+// whose own previous stage that round was; otherwise (p.tagged) the consumer first waits for
+// its stage's tag in the slot, written by the producer only once the previous round was
+// consumed. The plan asks nstage >= (NC - 1) * CH + 1, so that the producer, issuing in order,
+// can have every consumer's next stage in flight.
 int plan(Params& p, bool is_w4, int nt8, int nc, int sz_bytes) {
   const int KB = p.K / 128;
   const int rows_x = 8 * nt8;
@@ -1567,6 +1579,7 @@ int plan(Params& p, bool is_w4, int nt8, int nc, int sz_bytes) {
     const int ring_off = (fixed + 127) & ~127;
     const int nstage = min(MAX_STAGES, (SMEM_CAP - ring_off) / sb);
     if (nstage >= max(2, (nc - 1) * ch + 1)) {
+      p.tagged = (nstage % (nc * ch)) != 0;
       p.kps = kps;
       p.stage_bytes = sb;
       p.nstage = nstage;
