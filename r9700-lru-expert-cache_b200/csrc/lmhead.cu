@@ -1360,10 +1360,10 @@ __global__ void __launch_bounds__(128) p2p_combine_kernel(const float* __restric
   if (!ok && (threadIdx.x & 31) == 0) atomicExch(&g_lmhead_err, 2);
 }
 
-// Final (max, first argmax, logsumexp) of token blockIdx.x from its `nslots` partials: the max
-// and the smallest index attaining it first, then sum_i s_i exp(m_i - max) as independent terms
-// (no chain of rescalings), each in a fixed reduction order. 256 threads; the programmatic
-// dependent of the GEMM kernel.
+// Final (max, first argmax, logsumexp) of token blockIdx.x from its `nslots` partials: per warp
+// the max, the smallest index attaining it and sum_i s_i exp(m_i - warp max) as independent
+// terms, then the eight warps merged in order (one rescaling each); every reduction in a fixed
+// order. 256 threads; the programmatic dependent of the GEMM kernel.
 // With g_cta > 0 (the tcgen05 path) slots [0, g_cta) are the GEMM CTAs' and slots
 // g_cta + 2c + g the blocks of the split pair CTA c begins (valid only where it begins one).
 __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots, int g_cta) {
@@ -1374,7 +1374,6 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots, 
   __shared__ unsigned long long s_w[P2P_MAX_WORLD][P2P_WORDS];
   const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   griddep_launch_dependents();              // a peer-memory combine may launch behind it
-  griddep_wait();
   const float* base = p.partial + (long long)m * nslots * 3;
   const int KBS = p.K / 128, nblk = p.N / 128;
   const long long LU = (long long)((nblk + 1) / 2) * KBS;
@@ -1385,15 +1384,22 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots, 
     const int j = i - g_cta;
     return tc_begins_split(LU, g_cta, KBS, j >> 1, pair) && 2 * pair + (j & 1) < nblk;
   };
+  // which of this thread's slots hold data depends only on the launch shape: decided while
+  // the GEMM still runs, so that only the loads follow the wait
+  bool v[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) v[k] = valid(threadIdx.x + 256 * k);
+  griddep_wait();
+  // the error word travels with the partials (one round trip), not after the reductions
+  const int err = (threadIdx.x == 0) ? *reinterpret_cast<volatile int*>(&g_lmhead_err) : 0;
   float pm[2], ps[2];
   int pi[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int i = threadIdx.x + 256 * k;
-    const bool v = valid(i);
-    pm[k] = v ? __ldcg(base + 3 * i) : -INFINITY;
-    pi[k] = v ? __float_as_int(__ldcg(base + 3 * i + 1)) : 0x7fffffff;
-    ps[k] = v ? __ldcg(base + 3 * i + 2) : 0.f;
+    pm[k] = v[k] ? __ldcg(base + 3 * i) : -INFINITY;
+    pi[k] = v[k] ? __float_as_int(__ldcg(base + 3 * i + 1)) : 0x7fffffff;
+    ps[k] = v[k] ? __ldcg(base + 3 * i + 2) : 0.f;
   }
   for (int i = threadIdx.x + 512; i < nslots; i += 256) {      // more than 512 slots: fold in
     if (!valid(i)) continue;
@@ -1403,46 +1409,46 @@ __global__ void __launch_bounds__(256) stats_merge_kernel(Params p, int nslots, 
     a = b200::rowstat_merge(a, b);
     pm[1] = a.m; pi[1] = a.idx; ps[1] = a.s;
   }
-  // max and first index at it
-  float mx = fmaxf(pm[0], pm[1]);
+  // per warp: its max, the first index at it and the sum of exp(m_i - its max), each by a fixed
+  // shuffle tree; thread 0 then merges the eight warps in order (one barrier)
+  float wm = fmaxf(pm[0], pm[1]);
 #pragma unroll
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) s_m[warp] = mx;
-  __syncthreads();
-  mx = s_m[0];
-#pragma unroll
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_m[w]);
+  for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
   int id = 0x7fffffff;
 #pragma unroll
   for (int k = 0; k < 2; ++k)
-    if (pm[k] == mx && ps[k] > 0.f) id = min(id, pi[k]);
+    if (pm[k] == wm && ps[k] > 0.f) id = min(id, pi[k]);
 #pragma unroll
   for (int o = 16; o; o >>= 1) id = min(id, __shfl_xor_sync(0xffffffffu, id, o));
   float sum = 0.f;
 #pragma unroll
   for (int k = 0; k < 2; ++k)
-    if (ps[k] > 0.f) sum += ps[k] * __expf(pm[k] - mx);
+    if (ps[k] > 0.f) sum += ps[k] * __expf(pm[k] - wm);
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) {
+    s_m[warp] = wm;
     s_i[warp] = id;
     s_s[warp] = sum;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    float mx = s_m[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_m[w]);
     float t = 0.f;
     int best = 0x7fffffff;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      t += s_s[w];
-      best = min(best, s_i[w]);
+      if (s_s[w] > 0.f) t += s_s[w] * __expf(s_m[w] - mx);
+      if (s_m[w] == mx) best = min(best, s_i[w]);
     }
     float lse = mx + logf(t);
     long long arg = best;
     // A pipeline wait that ran out (this call or an earlier one not yet cleared with
     // b200_lmhead_error(1)) leaves some blocks unwritten: the statistics say so instead of
     // carrying a plausible value (max and logsumexp NaN, argmax -1).
-    if (*reinterpret_cast<volatile int*>(&g_lmhead_err) != 0) {
+    if (err != 0) {
       mx = __int_as_float(0x7fffffff);
       lse = mx;
       arg = -1;
