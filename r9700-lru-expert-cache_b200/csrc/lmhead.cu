@@ -377,7 +377,7 @@ constexpr int GEMV_TAGS = 320;
 constexpr int GEMV_HDR_RED = 384;
 __host__ __device__ constexpr int gemv_hdr(int nc) { return GEMV_HDR_RED + nc * MAXM * 12 + 16; }
 
-template <int KIND, int NT8, bool STATS, int NC>
+template <int KIND, int NT8, bool STATS, int NC, bool TAGGED>
 __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
   extern __shared__ __align__(128) char sm[];
   constexpr bool IS_W4 = kind_w4(KIND);
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
           ok = false;
           break;
         }
-        if (p.tagged) b200::tag_publish(&tag[slot], q);
+        if (TAGGED) b200::tag_publish(&tag[slot], q);
         const int strip = s0 + q / CH, ch = q % CH;
         const int kb0 = ch * p.kps, nkb = min(p.kps, KB - kb0);
         const long long blk = (long long)strip * KB + kb0;
@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(32 * (NC + 1), 1) gemv_kernel(Params p) {
         const int q = ls * CH + ch, slot = q % p.nstage;
         // (tagged ring) the stage is in its slot, so the parity wait cannot end on the slot's
         // previous round, whose copy may still be landing; then it has landed
-        const bool got = (!p.tagged || b200::tag_wait_bounded(&tag[slot], q, deadline)) &&
+        const bool got = (!TAGGED || b200::tag_wait_bounded(&tag[slot], q, deadline)) &&
                          b200::mbar_wait_bounded(&full[slot], (q / p.nstage) & 1, deadline);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
@@ -1566,10 +1566,10 @@ int allow_full_smem(const void* kern, bool (&done)[HOST_MAX_DEVICES]) {
 // a slot by the parity of the stage's round. That wait must not end on the slot's previous
 // round, whose copy may still be landing (issued is not enough: two bulk copies may complete
 // out of order). When nstage is a multiple of NC * CH every slot is owned by one consumer,
-// whose own previous stage that round was; otherwise (p.tagged) the consumer first waits for
-// its stage's tag in the slot, written by the producer only once the previous round was
-// consumed. The plan asks nstage >= (NC - 1) * CH + 1, so that the producer, issuing in order,
-// can have every consumer's next stage in flight.
+// whose own previous stage that round was; otherwise (p.tagged: the kernel's TAGGED
+// instantiation) the consumer first waits for its stage's tag in the slot, written by the
+// producer only once the previous round was consumed. The plan asks nstage >= (NC - 1) * CH
+// + 1, so that the producer, issuing in order, can have every consumer's next stage in flight.
 int plan(Params& p, bool is_w4, int nt8, int nc, int sz_bytes) {
   const int KB = p.K / 128;
   const int rows_x = 8 * nt8;
@@ -1621,9 +1621,9 @@ int launch_one(Params p, cudaStream_t stream) {
   constexpr int NC = IS_W4 ? (NT8 == 1 ? NC_W4 : NC_W4_WIDE) : NC_FP8;
   const int smem = plan(p, IS_W4, NT8, NC, IS_W4 ? kind_sz_bytes(KIND) : 0);
   if (smem < 0) return -8;
-  auto kern = gemv_kernel<KIND, NT8, STATS, NC>;
-  static bool smem_set[HOST_MAX_DEVICES] = {};
-  const int e = allow_full_smem((const void*)kern, smem_set);
+  auto kern = p.tagged ? gemv_kernel<KIND, NT8, STATS, NC, true> : gemv_kernel<KIND, NT8, STATS, NC, false>;
+  static bool smem_set[2][HOST_MAX_DEVICES] = {};
+  const int e = allow_full_smem((const void*)kern, smem_set[p.tagged ? 1 : 0]);
   if (e != 0) return e;
   const int grid = min(p.N / 16, num_sms());
   const int rc = launch_ex(kern, dim3(grid), dim3(32 * (NC + 1)), smem, stream, p.pdl != 0, p);
