@@ -1739,8 +1739,13 @@ int launch_tc_t(Params p, const uint8_t* qx_in, const float* xs_in, cudaStream_t
   uint8_t* qt = reinterpret_cast<uint8_t*>(base + QT_OFF);
   float* xt = reinterpret_cast<float*>(base + XT_OFF);
   p.px = reinterpret_cast<float*>(base + PX_OFF);
-  const long long units = (long long)(p.N / 256 + (p.N / 128) % 2) * KB;
-  const int grid = (int)std::min<long long>(units, std::min(num_sms(), TC_MAX_GRID));
+  const long long npairs = p.N / 256 + (p.N / 128) % 2, units = npairs * KB;
+  // At most one pair per SM (a vocabulary shard of up to ~38k rows): one whole pair per CTA, so
+  // no pair is split and no CTA pays the split pairs' ticket, partial exchange and second
+  // finish, which at that size cost more than the SMs left idle. Otherwise stream-K over
+  // every SM.
+  const int cap = std::min(num_sms(), TC_MAX_GRID);
+  const int grid = (int)(npairs <= cap ? npairs : std::min<long long>(units, cap));
   if (units * grid >= (1LL << 31)) return -8;               // the kernels' work arithmetic is 32-bit
   p.flags = reinterpret_cast<int*>(base + FLAG_OFF);
   int rc = launch_ex(act_tiles_kernel, dim3(KB, TPAD / 8), dim3(128), 0, stream, false,

@@ -314,7 +314,7 @@ def test_fp8_tc_split_pairs_with_busy_sms(cuda):
     are finished by whichever CTA arrives last, which waits only for CTAs already running, so
     the call completes, with the error word clear and every output identical, bit for bit, to
     the same call made alone."""
-    N, K, M = 128 * 75, 2560, 64                   # 38 pairs x 20 K-blocks over the SMs: splits
+    N, K, M = 128 * 301, 2560, 64                  # 151 pairs x 20 K-blocks over 148 SMs: splits
     wq, ws, _ = _fp8_weight(N, K, 21, cuda)
     x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
     ref = F8.fp8_lmhead(x, wq, ws)
@@ -339,8 +339,9 @@ def test_fp8_tc_work_splits(cuda, nblk):
     """Vocabulary sizes around the tcgen05 work split on 148 SMs (whole pairs per CTA, the rest
     split by 128-K units): a pair count that is a multiple of the CTA count (296 blocks = 148
     pairs), one pair more (298 blocks), odd block counts (297, 301), several extra pairs (447,
-    1187: the full head) and fewer pairs than CTAs (8, 3 blocks). Logits within the reference bound,
-    statistics against the oracle, repeated calls identical."""
+    1187: the full head) and fewer pairs than SMs (8, 3 blocks: one whole pair per CTA, none
+    split). Logits within the reference bound, statistics against the oracle, repeated calls
+    identical."""
     N, K, M = 128 * nblk, 2560, 64
     wq, ws, wdq = _fp8_weight(N, K, nblk, cuda)
     g = torch.Generator(device=cuda).manual_seed(10_000 + nblk)       # not the weight's stream
