@@ -436,6 +436,25 @@ def ops_bench(P, dev) -> dict:
         gbs = fp8_bytes(N_VOCAB, K_HID, M) / us / 1e3
         res[f"fp8_lmhead_M{M}"] = {"us_per_call": us, "GB_s": gbs, "frac_hbm": gbs / pk}
     del pool
+    # the headline's per-rank launch set at N = 2 / 4 / 8 (the largest vocabulary shard, the
+    # one the max over ranks sees), alone on this GPU: how much of a sharded step is the head
+    shards = {}
+    x64 = torch.randn(M_ROWS, K_HID, device=dev, dtype=torch.bfloat16)
+    for world in (2, 4, 8):
+        rows = max(b - a for a, b in P.sharded.vocab_shards(N_VOCAB, world))
+        spool = make_fp8_pool(P, rows, dev, 1)
+        it = {"i": 0}
+
+        def scall():
+            wq, ws = spool[it["i"] % len(spool)]
+            it["i"] += 1
+            P.fp8_target_lmhead.fp8_lmhead(x64, wq, ws)
+        us = time_graph(scall, 2 * len(spool), dev)
+        gbs = fp8_bytes(rows, K_HID, M_ROWS) / us / 1e3
+        shards[f"N{world}"] = {"rows": rows, "blocks": rows // 128, "us_per_call": us, "GB_s": gbs,
+                               "frac_hbm": gbs / pk}
+        del spool
+    res["fp8_lmhead_M64_rank_shard"] = shards
     w = (torch.randn(N_VOCAB, K_HID, device=dev) * 0.02).bfloat16()
     packed = [P.draft_w4_lmhead.pack_w4a16(w)]
     del w
